@@ -1,0 +1,261 @@
+/*
+ * spmm_c.h -- C ABI of the B200 SpMM engine (libspmm_b200.so).
+ *
+ * Computes C[M x N] = A[M x K] * B[K x N] with A sparse (CSR FP32, or BSR 16x16 FP16/BF16)
+ * and B, C dense row-major. Plain C: POD views, plain pointers and sizes, an opaque
+ * `void* stream` (a cudaStream_t; NULL = legacy default stream). No C++ types cross this
+ * boundary, so cgo / ctypes / JNI bindings can be written directly against it.
+ *
+ * Every entry point returns an int status: SPMM_OK (0) or a negative SPMM_ERR_* code
+ * (spmm_status_string() names it). Nothing prints or exits; the C++ API in include/spmm/
+ * maps the codes back to the reference's exit/throw behaviour.
+ *
+ * Each declaration cites the reference interface it replaces as
+ * (reference: <path in Adityaa-Saha17/Sparse-Matrix-Multiplication>:<line>).
+ */
+#ifndef SPMM_C_H
+#define SPMM_C_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define SPMM_OK 0
+#define SPMM_ERR_INVALID_ARG (-1)  /* bad size, null pointer, malformed CSR/BSR            */
+#define SPMM_ERR_MISALIGNED (-2)   /* an operand's alignment / N does not fit this path    */
+#define SPMM_ERR_CUDA (-3)         /* a CUDA runtime call failed                           */
+#define SPMM_ERR_NCCL (-4)         /* an NCCL call failed                                  */
+#define SPMM_ERR_TIMEOUT (-5)      /* a device-side wait ran out of its iteration budget   */
+#define SPMM_ERR_UNSUPPORTED (-6)  /* no device / feature for this request                 */
+#define SPMM_ERR_NO_MEMORY (-7)    /* host or device allocation failed                     */
+#define SPMM_ERR_BAD_INDEX (-8)    /* the device saw an index outside its declared range   */
+#define SPMM_ERR_IO (-9)           /* file open / short read / short write                 */
+#define SPMM_ERR_TOO_LARGE (-10)   /* the request exceeds a fixed capacity                 */
+
+const char* spmm_status_string(int status);
+int spmm_version(void); /* major*10000 + minor*100 + patch */
+
+/* ---------------------------------------------------------------- formats */
+
+/* Read-only CSR view (0-based, int32 indices, columns sorted within a row).
+ * (reference: src/csr.h:7-14, struct spmm::CSR) */
+typedef struct spmm_csr_view {
+    int32_t rows, cols, nnz;
+    const int32_t* row_ptr; /* rows + 1 */
+    const int32_t* col_idx; /* nnz */
+    const float* values;    /* nnz */
+} spmm_csr_view;
+
+/* Host CSR whose arrays the library malloc'd; release with spmm_csr_host_free. */
+typedef struct spmm_csr_host {
+    int32_t rows, cols, nnz;
+    int32_t* row_ptr;
+    int32_t* col_idx;
+    float* values;
+} spmm_csr_host;
+
+#define SPMM_DTYPE_F16 0
+#define SPMM_DTYPE_BF16 1
+
+/* BSR with 16x16 blocks; block b holds values[b*256 .. b*256+255], row-major inside the
+ * block, as FP16 or BF16 bits. (reference: src/bsr.h:22-60, BSR_BLOCK / BSR_host / BSR) */
+typedef struct spmm_bsr_view {
+    int32_t rows, cols;             /* original M, K                       */
+    int32_t block_rows, block_cols; /* ceil(M/16), ceil(K/16)              */
+    int32_t num_blocks;             /* non-empty blocks                    */
+    int32_t nnz;                    /* original nonzeros                   */
+    const int32_t* row_ptr;         /* block_rows + 1                      */
+    const int32_t* col_idx;         /* num_blocks, sorted per block-row    */
+    const uint16_t* values;         /* num_blocks * 256                    */
+    int32_t dtype;                  /* SPMM_DTYPE_F16 / SPMM_DTYPE_BF16    */
+} spmm_bsr_view;
+
+typedef struct spmm_bsr_host {
+    int32_t rows, cols, block_rows, block_cols, num_blocks, nnz, dtype;
+    int32_t* row_ptr;
+    int32_t* col_idx;
+    uint16_t* values;
+} spmm_bsr_host;
+
+/* (reference: src/bsr.h:62-68, struct spmm::BSR_stats) */
+typedef struct spmm_bsr_stats {
+    int32_t num_blocks;
+    int64_t stored_elements;
+    int32_t original_nnz;
+    double fill_in_ratio;
+    double block_density;
+} spmm_bsr_stats;
+
+/* ---------------------------------------------------------------- host utilities */
+
+/* (reference: src/csr.h:17-18, csr_alloc_host / csr_free_host) */
+int spmm_csr_host_alloc(int32_t rows, int32_t cols, int32_t nnz, spmm_csr_host* out);
+void spmm_csr_host_free(spmm_csr_host* m);
+
+/* COO -> CSR, sorted by (row, col); duplicates are kept, as the reference does.
+ * (reference: src/csr.h:20-21, csr_from_coo_host; src/csr.cu:44-72) */
+int spmm_csr_from_coo_host(int32_t rows, int32_t cols, int32_t n, const int32_t* row_idx,
+                           const int32_t* col_idx, const float* values, spmm_csr_host* out);
+
+/* Uniform Bernoulli(density) CSR from mt19937(seed), bit-identical to the reference
+ * generator's output. (reference: src/csr.h:23-25; src/csr.cu:74-103) */
+int spmm_generate_uniform_csr(int32_t rows, int32_t cols, float density, int32_t seed,
+                              spmm_csr_host* out);
+
+/* Dense rows x cols row-major U[-1,1) from mt19937(seed).
+ * (reference: src/bench/harness.cu:114-120, generate_dense_row_major) */
+int spmm_generate_dense(int32_t rows, int32_t cols, int32_t seed, float* out);
+
+/* Rows [row_begin, row_end) of a host CSR, row_ptr rebased to 0.
+ * (reference: src/csr.h:27-30, csr_row_slice_host; src/csr.cu:105-123) */
+int spmm_csr_row_slice_host(const spmm_csr_view* m, int32_t row_begin, int32_t row_end,
+                            spmm_csr_host* out);
+
+/* Binary CSR file: int32 rows, cols, nnz; row_ptr; col_idx; float values (little endian).
+ * (reference: src/csr.h:32-35; src/csr.cu:125-150) */
+int spmm_csr_read_binary(const char* path, spmm_csr_host* out);
+int spmm_csr_write_binary(const spmm_csr_view* m, const char* path);
+
+/* Structural check of a host CSR (row_ptr[0]==0, monotone, row_ptr[rows]==nnz,
+ * 0 <= col < cols). Returns SPMM_OK or SPMM_ERR_INVALID_ARG; *bad_row gets the first
+ * offending row (or -1). Not in the reference (it trusts its inputs). */
+int spmm_csr_validate_host(const spmm_csr_view* m, int32_t* bad_row);
+
+/* CSR -> BSR-16 on the host, bit-identical to the reference conversion (FP16: RN-even;
+ * BF16: RN-even). (reference: src/bsr.h:71-73, bsr_from_csr_host; src/bsr.cu:30-109) */
+int spmm_csr_to_bsr16_host(const spmm_csr_view* A, int32_t dtype, spmm_bsr_host* out);
+void spmm_bsr_host_free(spmm_bsr_host* b);
+
+/* (reference: src/bsr.h:79-80, bsr_compute_stats; src/bsr.cu:149-162) */
+int spmm_bsr_compute_stats(const spmm_bsr_view* b, spmm_bsr_stats* out);
+
+/* nnz-balanced row partition into G ranges: out[0..G], out[g]..out[g+1] is range g.
+ * Bit-identical to the reference's partition. (reference: src/spmm_multigpu.cu:26-40) */
+int spmm_nnz_balanced_bounds(const int32_t* row_ptr, int32_t rows, int64_t nnz, int32_t G,
+                             int32_t* out);
+
+/* ---------------------------------------------------------------- device compute */
+
+/* CSR algorithms (all compute the same product; they differ in work distribution). */
+#define SPMM_CSR_AUTO 0     /* = SPMM_CSR_MERGE                                            */
+#define SPMM_CSR_ROWWARP 1  /* one warp per row, vectorised B-row loads, no row splitting  */
+#define SPMM_CSR_MERGE 2    /* nnz-balanced merge-path chunks; long rows split + fix-up   */
+
+/* Tuning knobs; zero fields take the library default. chunk = merge-path items per warp
+ * (a multiple of 32, 64..8192); it also sets the long-row threshold. */
+typedef struct spmm_csr_tuning {
+    int32_t chunk;
+    int32_t col_pass; /* columns a warp covers per pass: 0 = auto, else 32/64/128/256 */
+    int32_t reserved[6];
+} spmm_csr_tuning;
+
+/* C = A * B, FP32, on `stream`; A, B, C are device pointers. Asynchronous.
+ * Per output element the sum runs in nonzero order with FP32 FMA (the reference's
+ * semantics); a row longer than the chunk is cut at merge-path chunk boundaries and its
+ * pieces are added left to right (deterministic, run to run and across streams).
+ * Uses a library-owned per-device workspace (allocated on first use, grown on demand);
+ * calls that use it concurrently on different streams of one device race -- use
+ * spmm_csr_f32_ws for that.
+ * (reference: the 7 launchers `void spmm_X(const CSR&, const float*, float*, int)`,
+ *  src/kernels/spmm_baseline.h:16 ... src/kernels/spmm_tiled_v4.h:63) */
+int spmm_csr_f32(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
+                 void* stream);
+
+/* Same, with explicit tuning and a caller-owned workspace. ws_bytes must be at least
+ * spmm_csr_f32_workspace_size(); the workspace must be all-zero before its first use and
+ * is left all-zero by every call. ws may be NULL when the size is 0. */
+int spmm_csr_f32_workspace_size(const spmm_csr_view* A, int32_t N, int32_t algo,
+                                const spmm_csr_tuning* tune, size_t* bytes);
+int spmm_csr_f32_ws(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
+                    const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, void* stream);
+
+/* Chunk size (merge-path items per warp) that the given call would use on the current
+ * device; rows longer than it are split at multiples of it (in row + nonzero index). */
+int spmm_csr_f32_chunk(const spmm_csr_view* A, int32_t N, int32_t algo,
+                       const spmm_csr_tuning* tune, int32_t* chunk);
+
+/* End-to-end call on HOST buffers: copies A and B to the current device (pinned or
+ * pageable host memory), computes, copies C back, synchronises `stream`. Device buffers
+ * are cached by the library between calls. */
+int spmm_csr_f32_host(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
+                      int32_t algo, void* stream);
+
+/* FP32 -> FP16 / BF16 (round to nearest even), n elements, device pointers.
+ * (reference: src/kernels/spmm_wmma.h:32, float_to_half) */
+int spmm_convert_f32(const float* src, uint16_t* dst, int64_t n, int32_t dtype, void* stream);
+
+/* BSR-16 x dense 16-bit B (same dtype as the blocks) -> FP32 C, on the tensor cores
+ * (tcgen05, TMEM accumulators). Device pointers. Asynchronous.
+ * (reference: src/kernels/spmm_wmma.h:39, spmm_wmma) */
+int spmm_bsr16(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, void* stream);
+
+/* BSR-16 path variants for measurement: 0 = auto, 1 = tcgen05, 2 = CUDA-core fallback. */
+int spmm_bsr16_algo(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, int32_t algo,
+                    void* stream);
+
+/* First error recorded by a kernel on `device` since the last clear (SPMM_OK if none):
+ * bad index, device wait timeout. Synchronises the device. *detail gets the offending
+ * index / site. clear != 0 resets the record. */
+int spmm_device_error(int32_t device, int32_t* code, int64_t* detail, int32_t clear);
+
+/* ---------------------------------------------------------------- hybrid dispatch */
+
+#define SPMM_BACKEND_CSR 0 /* CUDA-core CSR (the reference's Backend::CSR_TILED)   */
+#define SPMM_BACKEND_TC 1  /* BSR-16 tensor cores (the reference's TENSOR_WMMA)     */
+
+/* (reference: src/spmm_hybrid.h:33-40, struct HybridPlan) */
+typedef struct spmm_hybrid_plan {
+    int32_t backend;
+    double fill_in_ratio;
+    double block_density;
+    float threshold;
+    int32_t n_aligned;
+    const char* reason; /* static string */
+} spmm_hybrid_plan;
+
+/* Default fill-in threshold of this build (the reference's default is 2.0). */
+float spmm_hybrid_default_threshold(void);
+
+/* TC iff N % 16 == 0 && N > 0 && fill_in <= threshold. threshold <= 0 selects the default.
+ * (reference: src/spmm_hybrid.h:48, hybrid_choose; src/spmm_hybrid.cu:32-56) */
+int spmm_hybrid_choose(const spmm_csr_view* hA, int32_t N, float threshold,
+                       spmm_hybrid_plan* out);
+
+/* (reference: src/spmm_hybrid.h:51, backend_name) */
+const char* spmm_backend_name(int32_t backend);
+
+/* Host A/B/C; warmup + iters launches on the current device; *ms = median kernel time.
+ * (reference: src/spmm_hybrid.h:62-64, spmm_hybrid_run; src/spmm_hybrid.cu:58-125) */
+int spmm_hybrid_run(const spmm_hybrid_plan* plan, const spmm_csr_view* hA, const float* hB,
+                    float* hC, int32_t N, int32_t warmup, int32_t iters, float* ms);
+
+/* ---------------------------------------------------------------- multi-GPU */
+
+/* (reference: src/spmm_multigpu.h:32, gpu_count) */
+int spmm_gpu_count(void);
+
+/* nnz-balanced row split over num_gpus devices (clamped to the visible count), B copied
+ * to device 0 once and broadcast to the others with NCCL over NVLink, one host thread
+ * per device, row-disjoint C gathered into hC. *time_ms = max over devices of the median
+ * kernel time (the reference's semantics); *bcast_ms = the NCCL broadcast time.
+ * rows_out / nnz_out (may be NULL) receive num_gpus entries.
+ * (reference: src/spmm_multigpu.h:49-52, spmm_multigpu; src/spmm_multigpu.cu:44-120) */
+int spmm_multigpu_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
+                      int32_t num_gpus, int32_t warmup, int32_t iters, float* time_ms,
+                      int32_t* used_gpus, int32_t* rows_out, int32_t* nnz_out, float* bcast_ms);
+
+/* Managed-memory single-GPU path: A, B, C in cudaMallocManaged memory, prefetched to the
+ * current device. *ms = median kernel time.
+ * (reference: src/spmm_multigpu.h:57-58, spmm_unified; src/spmm_multigpu.cu:122-182) */
+int spmm_unified_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
+                     int32_t warmup, int32_t iters, float* ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPMM_C_H */

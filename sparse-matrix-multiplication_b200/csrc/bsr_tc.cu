@@ -1,0 +1,524 @@
+// BSR-16 x dense SpMM on the B200 tensor cores (tcgen05 MMA, TMEM accumulators, TMA).
+//
+// Replaces the reference's WMMA kernel (src/kernels/spmm_wmma.cu:49-142): same product,
+// C[M x N] (FP32) = A (BSR, 16x16 FP16/BF16 blocks) * B (K x N, same 16-bit type), FP32
+// accumulation.
+//
+// Mapping. A 16-row block-row is too short for an MMA's M (64/128), so the kernel computes
+// the transposed tile: for block (br, bc)
+//     C[br*16 : +16, n0 : n0+128]^T  +=  B[bc*16 : +16, n0 : n0+128]^T  *  A_blk^T
+// i.e. one tcgen05.mma kind::f16 with M = 128 (a 128-column slice of C), N = 16 (the block's
+// 16 rows), K = 16 (the block's 16 columns). Operand A of the MMA is the B tile, read
+// MN-major from shared memory (128B swizzle); operand B is the BSR block itself, read K-major
+// (32B swizzle) -- exactly its row-major storage. The accumulator lives in TMEM: lane m =
+// column n0+m of C, columns 16j..16j+15 = the 16 rows of block-row j of the CTA.
+//
+// A CTA owns G consecutive block-rows and one 128-column slice of N. A producer warp merges
+// the G sorted block-column lists; for every distinct block-column it TMA-loads the B tile
+// once (2 boxes of 16 x 64) plus the blocks of the block-rows that contain it, and the MMA
+// warp issues one MMA per such block into that block-row's TMEM columns. So a B tile shared
+// by several block-rows (e.g. dense diagonal blocks larger than 16) crosses L2 once per CTA.
+// A 4-deep shared-memory ring with mbarriers decouples TMA and MMA; four epilogue warps move
+// TMEM -> registers -> coalesced FP32 stores.
+//
+// Every mbarrier wait is bounded (iteration count and %globaltimer); on expiry the kernel
+// records SPMM_ERR_TIMEOUT, stops issuing work, drains what it issued, frees its TMEM and
+// returns. No TMA multicast is used.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <climits>
+#include <cstdint>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace spmm_b200 {
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kColCache = 4096;       // block-column indices cached in shared memory per CTA
+constexpr int kTcThreads = 192;       // warp 0 TMA, warp 1 MMA + TMEM, warps 2..5 epilogue
+constexpr unsigned kFullMask = 0xffffffffu;
+constexpr int kDone = -1;
+constexpr unsigned long long kWaitNs = 500ull * 1000 * 1000;  // 0.5 s per wait
+
+struct BsrArgs {
+    int M, K, N;
+    int block_rows, block_cols, num_blocks;
+    const int* __restrict__ row_ptr;
+    const int* __restrict__ col_idx;
+    const uint16_t* __restrict__ values;
+    const uint16_t* __restrict__ B;
+    float* __restrict__ C;
+    int dtype;
+    DeviceErrorRecord* err;
+};
+
+template <int G>
+struct Layout {
+    static constexpr int kBTile = 4096;                    // 16 x 128 x 2 B, two SW128 boxes
+    static constexpr int kASlot = 512;                     // 16 x 16 x 2 B, SW32
+    static constexpr int kStage = kBTile + G * kASlot;     // multiple of 1024
+    static constexpr int kCols = kStages * kStage;         // int[kColCache]
+    static constexpr int kMeta = kCols + kColCache * 4;
+    // meta: full[kStages], empty[kStages], acc (u64); mask[kStages] (int); row_ptr[G+1];
+    //       tmem base; abort flag
+    static constexpr int kFull = kMeta;
+    static constexpr int kEmpty = kFull + 8 * kStages;
+    static constexpr int kAcc = kEmpty + 8 * kStages;
+    static constexpr int kMask = kAcc + 8;
+    static constexpr int kRp = kMask + 4 * kStages;
+    static constexpr int kTmem = kRp + 4 * (G + 1);
+    static constexpr int kAbort = kTmem + 4;
+    static constexpr int kBytes = kAbort + 4;
+    static constexpr int kDynamic = kBytes + 1024;         // room to align the base to 1 KB
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: true when the phase completed; false on timeout or when another role of the
+// CTA has already given up (abort flag).
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    const unsigned long long t0 = global_ns();
+    for (uint32_t it = 0; it < (1u << 26); ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63) == 63) {
+            if (*abort_flag) return false;
+            if (global_ns() - t0 > kWaitNs) return false;
+        }
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+        "[%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05 "version 1" format): start address, leading and
+// stride byte offsets (16-byte units), swizzle mode in bits 61..63.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint64_t swizzle) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr & 0x3ffffu) >> 4);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3fffu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3fffu) << 32;
+    d |= 1ull << 46;
+    d |= swizzle << 61;
+    return d;
+}
+
+constexpr uint64_t kSwizzle128 = 2;
+constexpr uint64_t kSwizzle32 = 6;
+
+// Instruction descriptor for kind::f16: D = F32, A and B the same 16-bit type, A MN-major,
+// B K-major, M = 128, N = 16.
+__device__ __forceinline__ uint32_t instr_desc(int dtype) {
+    const uint32_t fmt = dtype == SPMM_DTYPE_BF16 ? 1u : 0u;
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (0u << 16) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    bsr_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_a, BsrArgs a) {
+    using L = Layout<G>;
+    extern __shared__ uint8_t smem_raw[];
+    // 1 KB alignment (SW128 atoms) in the shared address space.
+    const uint32_t raw = smem_addr(smem_raw);
+    uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    const uint32_t sbase = smem_addr(base);
+
+    int* cols = reinterpret_cast<int*>(base + L::kCols);
+    int* masks = reinterpret_cast<int*>(base + L::kMask);
+    int* rp = reinterpret_cast<int*>(base + L::kRp);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + L::kTmem);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(base + L::kAbort);
+    const uint32_t full0 = sbase + L::kFull, empty0 = sbase + L::kEmpty, acc_bar = sbase + L::kAcc;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int br0 = blockIdx.x * G;
+    const int n0 = blockIdx.y * 128;
+
+    // Block-row extents and the group's block-column list (prefix up to kColCache).
+    if (threadIdx.x <= G) {
+        const int br = min(br0 + static_cast<int>(threadIdx.x), a.block_rows);
+        int v = __ldg(a.row_ptr + br);
+        v = max(0, min(v, a.num_blocks));
+        rp[threadIdx.x] = v;
+    }
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        mbar_init(acc_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(sbase + L::kTmem, G * 16 <= 32 ? 32 : (G * 16 <= 64 ? 64 : 128));
+    __syncthreads();
+    // Monotone block-row extents.
+    const int lo = rp[0];
+    int hi = lo;
+    for (int j = 1; j <= G; ++j) hi = max(hi, rp[j]);
+    for (int i = threadIdx.x; i < min(hi - lo, kColCache); i += kTcThreads) cols[i] = __ldg(a.col_idx + lo + i);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer: merge G block-column lists, TMA-load tiles
+        int cur = 0, end = 0;
+        if (lane < G) {
+            cur = rp[lane];
+            end = max(cur, rp[lane + 1]);
+        }
+        int step = 0;
+        bool ok = true;
+        while (ok) {
+            int my = INT_MAX;
+            if (lane < G && cur < end) {
+                const int off = cur - lo;
+                my = off < kColCache ? cols[off] : __ldg(a.col_idx + cur);
+                if (my < 0 || my >= a.block_cols) {
+                    record_device_error(a.err, SPMM_ERR_BAD_INDEX, cur);
+                    my = max(0, min(my, a.block_cols - 1));
+                }
+            }
+            const int bc = __reduce_min_sync(kFullMask, my);
+            const int s = step % kStages;
+            const uint32_t phase = (step / kStages) & 1u;
+            if (lane == 0) ok = mbar_wait(empty0 + 8 * s, phase ^ 1u, abort_flag);
+            ok = __shfl_sync(kFullMask, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            const uint32_t stage = sbase + s * L::kStage;
+            if (bc == INT_MAX) {
+                if (lane == 0) {
+                    masks[s] = kDone;
+                    mbar_arrive(full0 + 8 * s);
+                }
+                break;
+            }
+            const unsigned mask = __ballot_sync(kFullMask, lane < G && my == bc);
+            if (lane == 0) {
+                masks[s] = static_cast<int>(mask);
+                mbar_arrive_expect_tx(full0 + 8 * s, L::kBTile + __popc(mask) * L::kASlot);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                tma_load_2d(stage, &tmap_b, full0 + 8 * s, n0, bc * 16);
+                tma_load_2d(stage + 2048, &tmap_b, full0 + 8 * s, n0 + 64, bc * 16);
+            }
+            if ((mask >> lane) & 1u) {
+                tma_load_2d(stage + L::kBTile + lane * L::kASlot, &tmap_a, full0 + 8 * s, 0, cur * 16);
+                ++cur;
+            }
+            ++step;
+        }
+        if (!ok && lane == 0) {
+            *abort_flag = 1;
+            record_device_error(a.err, SPMM_ERR_TIMEOUT, 1);
+            // Let the copies issued for the last stages land before the CTA's shared memory
+            // is released (each wait is bounded again).
+            for (int t = max(0, step - kStages); t < step; ++t) {
+                const unsigned long long t0 = global_ns();
+                while (!mbar_try_wait(full0 + 8 * (t % kStages), (t / kStages) & 1u) && global_ns() - t0 < kWaitNs) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (one thread)
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(a.dtype);
+            unsigned started = 0;
+            bool ok = true;
+            for (int step = 0;; ++step) {
+                const int s = step % kStages;
+                const uint32_t phase = (step / kStages) & 1u;
+                if (!mbar_wait(full0 + 8 * s, phase, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const int mask = masks[s];
+                if (mask == kDone) break;
+                tc_fence_after();
+                const uint32_t stage = sbase + s * L::kStage;
+                const uint64_t adesc = smem_desc(stage, 2048, 1024, kSwizzle128);
+                for (int j = 0; j < G; ++j) {
+                    if (!((mask >> j) & 1)) continue;
+                    const uint64_t bdesc = smem_desc(stage + L::kBTile + j * L::kASlot, 16, 256, kSwizzle32);
+                    umma_f16(tmem + 16 * j, adesc, bdesc, idesc, (started >> j) & 1u);
+                    started |= 1u << j;
+                }
+                umma_commit(empty0 + 8 * s);
+            }
+            umma_commit(acc_bar);  // arrives when every MMA issued above has completed
+            if (!ok) {
+                *abort_flag = 1;
+                record_device_error(a.err, SPMM_ERR_TIMEOUT, 2);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: TMEM -> registers -> C
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const bool ok = __all_sync(kFullMask, mbar_wait(acc_bar, 0, abort_flag));
+        tc_fence_after();
+        const int col = n0 + q * 32 + lane;
+        for (int j = 0; j < G; ++j) {
+            const int br = br0 + j;
+            if (br >= a.block_rows) break;
+            uint32_t v[16];
+            const bool has = rp[j + 1] > rp[j];
+            if (ok && has) {
+                tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + 16 * j, v);
+            } else {
+#pragma unroll
+                for (int r = 0; r < 16; ++r) v[r] = 0u;
+            }
+            if (col < a.N) {
+#pragma unroll
+                for (int r = 0; r < 16; ++r) {
+                    const int row = br * 16 + r;
+                    if (row < a.M) __stcs(a.C + static_cast<size_t>(row) * a.N + col, __uint_as_float(v[r]));
+                }
+            }
+        }
+        if (!ok && lane == 0) record_device_error(a.err, SPMM_ERR_TIMEOUT, 3);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, G * 16 <= 32 ? 32 : (G * 16 <= 64 ? 64 : 128));
+    }
+}
+
+// CUDA-core BSR kernel: one CTA per (block-row, 128-column slice), a thread per column,
+// 16 row accumulators per thread, each block staged in shared memory as FP32.
+template <bool BF16>
+__global__ void __launch_bounds__(128) bsr_cudacore_kernel(BsrArgs a) {
+    __shared__ float As[256];
+    const int br = blockIdx.x;
+    const int n = blockIdx.y * 128 + threadIdx.x;
+    float acc[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+    const int b0 = max(0, min(__ldg(a.row_ptr + br), a.num_blocks));
+    const int b1 = max(b0, min(__ldg(a.row_ptr + br + 1), a.num_blocks));
+    for (int b = b0; b < b1; ++b) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < 256; i += 128) {
+            const uint16_t h = __ldg(a.values + static_cast<size_t>(b) * 256 + i);
+            if constexpr (BF16) As[i] = __uint_as_float(static_cast<uint32_t>(h) << 16);
+            else As[i] = __half2float(__ushort_as_half(h));
+        }
+        __syncthreads();
+        int bc = __ldg(a.col_idx + b);
+        if (bc < 0 || bc >= a.block_cols) {
+            if (threadIdx.x == 0) record_device_error(a.err, SPMM_ERR_BAD_INDEX, b);
+            continue;
+        }
+        if (n >= a.N) continue;
+        for (int k = 0; k < 16; ++k) {
+            const int kk = bc * 16 + k;
+            if (kk >= a.K) break;
+            const uint16_t h = __ldg(a.B + static_cast<size_t>(kk) * a.N + n);
+            float bv;
+            if constexpr (BF16) bv = __uint_as_float(static_cast<uint32_t>(h) << 16);
+            else bv = __half2float(__ushort_as_half(h));
+#pragma unroll
+            for (int r = 0; r < 16; ++r) acc[r] = fmaf(As[r * 16 + k], bv, acc[r]);
+        }
+    }
+    if (n < a.N) {
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int row = br * 16 + r;
+            if (row < a.M) a.C[static_cast<size_t>(row) * a.N + n] = acc[r];
+        }
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+              uint32_t box_outer, CUtensorMapSwizzle swz) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return SPMM_ERR_UNSUPPORTED;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? SPMM_OK : SPMM_ERR_INVALID_ARG;
+}
+
+template <int G>
+int launch_tc(const BsrArgs& a, cudaStream_t s) {
+    CUtensorMap tb, ta;
+    SPMM_TRY(encode_2d(&tb, a.B, static_cast<uint64_t>(a.N), static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.N) * 2, 64,
+                       16, CU_TENSOR_MAP_SWIZZLE_128B));
+    SPMM_TRY(encode_2d(&ta, a.values, 16, static_cast<uint64_t>(a.num_blocks) * 16, 32, 16, 16,
+                       CU_TENSOR_MAP_SWIZZLE_32B));
+    using L = Layout<G>;
+    // Per device (the attribute belongs to the current device's context).
+    SPMM_CUDA_TRY(cudaFuncSetAttribute(bsr_tcgen05_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamic));
+    const dim3 grid((a.block_rows + G - 1) / G, (a.N + 127) / 128);
+    bsr_tcgen05_kernel<G><<<grid, kTcThreads, L::kDynamic, s>>>(tb, ta, a);
+    SPMM_CUDA_TRY(cudaGetLastError());
+    return SPMM_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+// algo: 0 auto, 1 tensor cores (error if the operands do not fit it), 2 CUDA cores.
+int bsr16_launch(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, int32_t algo, cudaStream_t s,
+                 DeviceState* st) {
+    if (!A || N < 0 || A->rows < 0 || A->cols < 0 || A->num_blocks < 0 || A->block_rows < 0) return SPMM_ERR_INVALID_ARG;
+    if (A->dtype != SPMM_DTYPE_F16 && A->dtype != SPMM_DTYPE_BF16) return SPMM_ERR_INVALID_ARG;
+    if (A->block_rows != (A->rows + 15) / 16 || A->block_cols != (A->cols + 15) / 16) return SPMM_ERR_INVALID_ARG;
+    if (algo < 0 || algo > 2) return SPMM_ERR_INVALID_ARG;
+    if (A->rows == 0 || N == 0) return SPMM_OK;
+    if (!C || !A->row_ptr || (A->num_blocks > 0 && (!A->col_idx || !A->values || !B16))) return SPMM_ERR_INVALID_ARG;
+    if (A->num_blocks > (1 << 26)) return SPMM_ERR_TOO_LARGE;
+    BsrArgs a{};
+    a.M = A->rows;
+    a.K = A->cols;
+    a.N = N;
+    a.block_rows = A->block_rows;
+    a.block_cols = A->block_cols;
+    a.num_blocks = A->num_blocks;
+    a.row_ptr = A->row_ptr;
+    a.col_idx = A->col_idx;
+    a.values = A->values;
+    a.B = static_cast<const uint16_t*>(B16);
+    a.C = C;
+    a.dtype = A->dtype;
+    a.err = st->err;
+    const bool tc_ok = st->cc_major == 10 && N % 8 == 0 && A->num_blocks > 0 && A->cols > 0 && aligned16(B16) &&
+                       aligned16(A->values);
+    if (algo == 1 && !tc_ok) return SPMM_ERR_MISALIGNED;
+    if (algo != 2 && tc_ok) {
+        // Eight block-rows per CTA when that still fills the GPU, else four.
+        const long long ctas8 = static_cast<long long>((a.block_rows + 7) / 8) * ((N + 127) / 128);
+        if (ctas8 >= st->sm_count) return launch_tc<8>(a, s);
+        return launch_tc<4>(a, s);
+    }
+    const dim3 grid(a.block_rows, (N + 127) / 128);
+    if (a.dtype == SPMM_DTYPE_BF16) bsr_cudacore_kernel<true><<<grid, 128, 0, s>>>(a);
+    else bsr_cudacore_kernel<false><<<grid, 128, 0, s>>>(a);
+    SPMM_CUDA_TRY(cudaGetLastError());
+    return SPMM_OK;
+}
+
+}  // namespace spmm_b200
+
+using namespace spmm_b200;
+
+extern "C" {
+
+int spmm_bsr16_algo(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, int32_t algo, void* stream) {
+    DeviceState* st = nullptr;
+    SPMM_TRY(current_device_state(&st));
+    return bsr16_launch(A, B16, C, N, algo, as_stream(stream), st);
+}
+
+int spmm_bsr16(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, void* stream) {
+    return spmm_bsr16_algo(A, B16, C, N, 0, stream);
+}
+
+}  // extern "C"

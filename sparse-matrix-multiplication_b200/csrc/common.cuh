@@ -1,0 +1,72 @@
+// Internal helpers shared by the CUDA translation units of libspmm_b200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+
+#include "spmm_c.h"
+
+namespace spmm_b200 {
+
+// Return SPMM_ERR_CUDA from the enclosing function when a runtime call fails.
+#define SPMM_CUDA_TRY(call)                                     \
+    do {                                                        \
+        cudaError_t e__ = (call);                               \
+        if (e__ != cudaSuccess) {                               \
+            spmm_b200::note_cuda_error(e__, #call, __FILE__, __LINE__); \
+            return SPMM_ERR_CUDA;                               \
+        }                                                       \
+    } while (0)
+
+#define SPMM_TRY(call)              \
+    do {                            \
+        int s__ = (call);           \
+        if (s__ != SPMM_OK) return s__; \
+    } while (0)
+
+void note_cuda_error(cudaError_t e, const char* what, const char* file, int line);
+
+// Device-side error record: word 0 = status code (first writer wins), word 1..2 = detail.
+struct DeviceErrorRecord {
+    int code;
+    int pad;
+    long long detail;
+};
+
+__device__ __forceinline__ void record_device_error(DeviceErrorRecord* rec, int code, long long detail) {
+    if (rec && atomicCAS(&rec->code, 0, code) == 0) rec->detail = detail;
+}
+
+// Per-device state owned by the library. Created lazily by the first call on a device;
+// that first call allocates, so it must not be made inside a stream capture.
+struct DeviceState {
+    int device = -1;
+    int sm_count = 0;
+    int l2_bytes = 0;
+    int cc_major = 0, cc_minor = 0;
+    DeviceErrorRecord* err = nullptr;  // device memory, zeroed
+    // CSR workspace (all-zero between calls).
+    void* csr_ws = nullptr;
+    size_t csr_ws_bytes = 0;
+    // Cached device buffers of the host-buffer entry point.
+    void* h_rp = nullptr; size_t h_rp_bytes = 0;
+    void* h_ci = nullptr; size_t h_ci_bytes = 0;
+    void* h_v = nullptr;  size_t h_v_bytes = 0;
+    void* h_b = nullptr;  size_t h_b_bytes = 0;
+    void* h_c = nullptr;  size_t h_c_bytes = 0;
+    std::mutex mu;
+};
+
+// State of the current device (nullptr + status on failure).
+int current_device_state(DeviceState** out);
+int device_state(int device, DeviceState** out);
+
+// Grow `*buf` (device memory) to at least `bytes`; zero-fill when `zero` is set.
+int ensure_device_buffer(void** buf, size_t* cur, size_t bytes, bool zero, cudaStream_t stream);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace spmm_b200

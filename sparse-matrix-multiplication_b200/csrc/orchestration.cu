@@ -1,0 +1,528 @@
+// Host-side orchestration of libspmm_b200.so: the host-buffer end-to-end call, hybrid
+// CUDA-core / tensor-core dispatch, the multi-GPU row split with an NCCL broadcast of B,
+// and the managed-memory path.
+//
+//   hybrid      src/spmm_hybrid.cu:28-125
+//   multi-GPU   src/spmm_multigpu.cu:44-120
+//   unified     src/spmm_multigpu.cu:122-182
+
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "common.cuh"
+
+namespace spmm_b200 {
+
+// NCCL is resolved at run time (dlopen of libnccl.so.2) rather than linked: a process that
+// already holds an NCCL (e.g. the one PyTorch ships) keeps using it, and loading this library
+// never changes which NCCL the rest of the process sees.
+struct NcclApi {
+    ncclResult_t (*comm_init_all)(ncclComm_t*, int, const int*) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    bool ok = false;
+};
+
+const NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.comm_init_all = reinterpret_cast<decltype(api.comm_init_all)>(dlsym(h, "ncclCommInitAll"));
+        api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
+        api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
+        api.broadcast = reinterpret_cast<decltype(api.broadcast)>(dlsym(h, "ncclBroadcast"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        api.ok = api.comm_init_all && api.group_start && api.group_end && api.broadcast && api.comm_destroy;
+    });
+    return api;
+}
+
+int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
+                   const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream, DeviceState* st);
+int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, const spmm_csr_tuning* tune,
+                            int sm_count, size_t* bytes);
+
+namespace {
+
+float median(std::vector<float> v) {
+    if (v.empty()) return 0.f;
+    std::sort(v.begin(), v.end());
+    return v[v.size() / 2];
+}
+
+// Device copies of one CSR matrix.
+struct DeviceCsr {
+    int* rp = nullptr;
+    int* ci = nullptr;
+    float* v = nullptr;
+    spmm_csr_view view{};
+    ~DeviceCsr() {
+        cudaFree(rp);
+        cudaFree(ci);
+        cudaFree(v);
+    }
+};
+
+int upload_csr(const spmm_csr_view* h, DeviceCsr* d, cudaStream_t s) {
+    SPMM_CUDA_TRY(cudaMalloc(&d->rp, sizeof(int) * (static_cast<size_t>(h->rows) + 1)));
+    SPMM_CUDA_TRY(cudaMalloc(&d->ci, sizeof(int) * std::max<size_t>(h->nnz, 1)));
+    SPMM_CUDA_TRY(cudaMalloc(&d->v, sizeof(float) * std::max<size_t>(h->nnz, 1)));
+    SPMM_CUDA_TRY(cudaMemcpyAsync(d->rp, h->row_ptr, sizeof(int) * (static_cast<size_t>(h->rows) + 1),
+                                  cudaMemcpyHostToDevice, s));
+    if (h->nnz) {
+        SPMM_CUDA_TRY(cudaMemcpyAsync(d->ci, h->col_idx, sizeof(int) * h->nnz, cudaMemcpyHostToDevice, s));
+        SPMM_CUDA_TRY(cudaMemcpyAsync(d->v, h->values, sizeof(float) * h->nnz, cudaMemcpyHostToDevice, s));
+    }
+    d->view = *h;
+    d->view.row_ptr = d->rp;
+    d->view.col_idx = d->ci;
+    d->view.values = d->v;
+    return SPMM_OK;
+}
+
+// Times warmup + iters launches of `fn` on `s` with events; returns the median in ms.
+template <typename F>
+int time_launches(F&& fn, int warmup, int iters, cudaStream_t s, float* ms_out) {
+    for (int i = 0; i < warmup; ++i) SPMM_TRY(fn());
+    SPMM_CUDA_TRY(cudaStreamSynchronize(s));
+    cudaEvent_t e0, e1;
+    SPMM_CUDA_TRY(cudaEventCreate(&e0));
+    SPMM_CUDA_TRY(cudaEventCreate(&e1));
+    std::vector<float> t;
+    int rc = SPMM_OK;
+    for (int i = 0; i < iters && rc == SPMM_OK; ++i) {
+        cudaEventRecord(e0, s);
+        rc = fn();
+        cudaEventRecord(e1, s);
+        if (cudaEventSynchronize(e1) != cudaSuccess) rc = SPMM_ERR_CUDA;
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        t.push_back(ms);
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms_out = median(t);
+    return rc;
+}
+
+bool check_host_view(const spmm_csr_view* A) {
+    return A && A->rows >= 0 && A->cols >= 0 && A->nnz >= 0 && (A->rows == 0 || A->row_ptr) &&
+           (A->nnz == 0 || (A->col_idx && A->values));
+}
+
+}  // namespace
+
+int bsr16_launch(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, int32_t algo, cudaStream_t s,
+                 DeviceState* st);
+
+}  // namespace spmm_b200
+
+using namespace spmm_b200;
+
+extern "C" {
+
+int spmm_csr_f32_host(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, int32_t algo, void* stream) {
+    if (!check_host_view(hA) || N < 0 || (hA->rows > 0 && N > 0 && !hC) || (hA->nnz > 0 && N > 0 && !hB))
+        return SPMM_ERR_INVALID_ARG;
+    DeviceState* st = nullptr;
+    SPMM_TRY(current_device_state(&st));
+    const cudaStream_t s = as_stream(stream);
+    const size_t M = hA->rows, K = hA->cols, nnz = hA->nnz;
+    size_t ws = 0;
+    SPMM_TRY(csr_f32_workspace_bytes(hA, N, algo, nullptr, st->sm_count, &ws));
+    std::lock_guard<std::mutex> lock(st->mu);
+    SPMM_TRY(ensure_device_buffer(&st->h_rp, &st->h_rp_bytes, sizeof(int) * (M + 1), false, s));
+    SPMM_TRY(ensure_device_buffer(&st->h_ci, &st->h_ci_bytes, sizeof(int) * std::max<size_t>(nnz, 1), false, s));
+    SPMM_TRY(ensure_device_buffer(&st->h_v, &st->h_v_bytes, sizeof(float) * std::max<size_t>(nnz, 1), false, s));
+    SPMM_TRY(ensure_device_buffer(&st->h_b, &st->h_b_bytes, sizeof(float) * std::max<size_t>(K * N, 1), false, s));
+    SPMM_TRY(ensure_device_buffer(&st->h_c, &st->h_c_bytes, sizeof(float) * std::max<size_t>(M * N, 1), false, s));
+    SPMM_TRY(ensure_device_buffer(&st->csr_ws, &st->csr_ws_bytes, ws, true, s));
+    SPMM_CUDA_TRY(cudaMemcpyAsync(st->h_rp, hA->row_ptr, sizeof(int) * (M + 1), cudaMemcpyHostToDevice, s));
+    if (nnz) {
+        SPMM_CUDA_TRY(cudaMemcpyAsync(st->h_ci, hA->col_idx, sizeof(int) * nnz, cudaMemcpyHostToDevice, s));
+        SPMM_CUDA_TRY(cudaMemcpyAsync(st->h_v, hA->values, sizeof(float) * nnz, cudaMemcpyHostToDevice, s));
+    }
+    if (K * N != 0) SPMM_CUDA_TRY(cudaMemcpyAsync(st->h_b, hB, sizeof(float) * K * N, cudaMemcpyHostToDevice, s));
+    spmm_csr_view d = *hA;
+    d.row_ptr = static_cast<int*>(st->h_rp);
+    d.col_idx = static_cast<int*>(st->h_ci);
+    d.values = static_cast<float*>(st->h_v);
+    SPMM_TRY(csr_f32_launch(&d, static_cast<float*>(st->h_b), static_cast<float*>(st->h_c), N, algo, nullptr,
+                            st->csr_ws, st->csr_ws_bytes, s, st));
+    if (M * N != 0) SPMM_CUDA_TRY(cudaMemcpyAsync(hC, st->h_c, sizeof(float) * M * N, cudaMemcpyDeviceToHost, s));
+    SPMM_CUDA_TRY(cudaStreamSynchronize(s));
+    return SPMM_OK;
+}
+
+// ------------------------------------------------------------------------ hybrid
+
+// Fill-in at or below which the tensor-core path is chosen.
+float spmm_hybrid_default_threshold(void) { return 2.0f; }
+
+const char* spmm_backend_name(int32_t b) { return b == SPMM_BACKEND_TC ? "wmma" : "csr"; }
+
+int spmm_hybrid_choose(const spmm_csr_view* hA, int32_t N, float threshold, spmm_hybrid_plan* out) {
+    if (!check_host_view(hA) || !out) return SPMM_ERR_INVALID_ARG;
+    if (!(threshold > 0.f)) threshold = spmm_hybrid_default_threshold();
+    out->threshold = threshold;
+    out->n_aligned = (N % 16 == 0) && (N > 0);
+    spmm_bsr_host b{};
+    SPMM_TRY(spmm_csr_to_bsr16_host(hA, SPMM_DTYPE_F16, &b));
+    spmm_bsr_view v{b.rows, b.cols, b.block_rows, b.block_cols, b.num_blocks, b.nnz, b.row_ptr, b.col_idx, b.values, b.dtype};
+    spmm_bsr_stats s{};
+    spmm_bsr_compute_stats(&v, &s);
+    spmm_bsr_host_free(&b);
+    out->fill_in_ratio = s.fill_in_ratio;
+    out->block_density = s.block_density;
+    const bool dense_blocks = s.fill_in_ratio <= threshold;
+    if (out->n_aligned && dense_blocks) {
+        out->backend = SPMM_BACKEND_TC;
+        out->reason = "low BSR fill-in and N aligned to 16 -> Tensor Cores";
+    } else if (!out->n_aligned) {
+        out->backend = SPMM_BACKEND_CSR;
+        out->reason = "N not a multiple of 16 -> CUDA-core CSR";
+    } else {
+        out->backend = SPMM_BACKEND_CSR;
+        out->reason = "high BSR fill-in -> CUDA-core CSR";
+    }
+    return SPMM_OK;
+}
+
+int spmm_hybrid_run(const spmm_hybrid_plan* plan, const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
+                    int32_t warmup, int32_t iters, float* ms) {
+    if (!plan || !check_host_view(hA) || N < 0 || warmup < 0 || iters < 1 || !ms) return SPMM_ERR_INVALID_ARG;
+    DeviceState* st = nullptr;
+    SPMM_TRY(current_device_state(&st));
+    cudaStream_t s = nullptr;
+    SPMM_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    const size_t M = hA->rows, K = hA->cols;
+    float* dB = nullptr;
+    float* dC = nullptr;
+    int rc = SPMM_OK;
+    auto fail = [&](int code) {
+        rc = code;
+        return code;
+    };
+    do {
+        if (cudaMalloc(&dB, sizeof(float) * std::max<size_t>(K * N, 1)) != cudaSuccess ||
+            cudaMalloc(&dC, sizeof(float) * std::max<size_t>(M * N, 1)) != cudaSuccess) {
+            fail(SPMM_ERR_NO_MEMORY);
+            break;
+        }
+        if (K * N != 0 && cudaMemcpyAsync(dB, hB, sizeof(float) * K * N, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+            fail(SPMM_ERR_CUDA);
+            break;
+        }
+        if (plan->backend == SPMM_BACKEND_TC) {
+            spmm_bsr_host hb{};
+            if (fail(spmm_csr_to_bsr16_host(hA, SPMM_DTYPE_F16, &hb)) != SPMM_OK) break;
+            int* brp = nullptr;
+            int* bci = nullptr;
+            uint16_t* bv = nullptr;
+            uint16_t* b16 = nullptr;
+            const size_t nb = hb.num_blocks;
+            if (cudaMalloc(&brp, sizeof(int) * (hb.block_rows + 1)) != cudaSuccess ||
+                cudaMalloc(&bci, sizeof(int) * std::max<size_t>(nb, 1)) != cudaSuccess ||
+                cudaMalloc(&bv, sizeof(uint16_t) * std::max<size_t>(nb * 256, 1)) != cudaSuccess ||
+                cudaMalloc(&b16, sizeof(uint16_t) * std::max<size_t>(K * N, 1)) != cudaSuccess) {
+                rc = SPMM_ERR_NO_MEMORY;
+            } else {
+                cudaMemcpyAsync(brp, hb.row_ptr, sizeof(int) * (hb.block_rows + 1), cudaMemcpyHostToDevice, s);
+                if (nb) {
+                    cudaMemcpyAsync(bci, hb.col_idx, sizeof(int) * nb, cudaMemcpyHostToDevice, s);
+                    cudaMemcpyAsync(bv, hb.values, sizeof(uint16_t) * nb * 256, cudaMemcpyHostToDevice, s);
+                }
+                rc = spmm_convert_f32(dB, b16, static_cast<int64_t>(K) * N, SPMM_DTYPE_F16, s);
+                if (rc == SPMM_OK) {
+                    spmm_bsr_view v{hb.rows, hb.cols, hb.block_rows, hb.block_cols, hb.num_blocks, hb.nnz, brp, bci, bv,
+                                    SPMM_DTYPE_F16};
+                    rc = time_launches([&] { return bsr16_launch(&v, b16, dC, N, 0, s, st); }, warmup, iters, s, ms);
+                }
+            }
+            cudaStreamSynchronize(s);
+            cudaFree(brp);
+            cudaFree(bci);
+            cudaFree(bv);
+            cudaFree(b16);
+            spmm_bsr_host_free(&hb);
+        } else {
+            DeviceCsr d;
+            if (fail(upload_csr(hA, &d, s)) != SPMM_OK) break;
+            size_t need = 0;
+            if (fail(csr_f32_workspace_bytes(hA, N, SPMM_CSR_AUTO, nullptr, st->sm_count, &need)) != SPMM_OK) break;
+            void* ws = nullptr;
+            if (need && cudaMalloc(&ws, need) != cudaSuccess) {
+                fail(SPMM_ERR_NO_MEMORY);
+                break;
+            }
+            if (need) cudaMemsetAsync(ws, 0, need, s);
+            rc = time_launches(
+                [&] { return csr_f32_launch(&d.view, dB, dC, N, SPMM_CSR_AUTO, nullptr, ws, need, s, st); }, warmup,
+                iters, s, ms);
+            cudaStreamSynchronize(s);
+            cudaFree(ws);
+        }
+        if (rc == SPMM_OK && M * N != 0 &&
+            cudaMemcpyAsync(hC, dC, sizeof(float) * M * N, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+            rc = SPMM_ERR_CUDA;
+        if (rc == SPMM_OK && cudaStreamSynchronize(s) != cudaSuccess) rc = SPMM_ERR_CUDA;
+    } while (false);
+    cudaStreamSynchronize(s);
+    cudaFree(dB);
+    cudaFree(dC);
+    cudaStreamDestroy(s);
+    return rc;
+}
+
+// ------------------------------------------------------------------------ multi-GPU
+
+int spmm_gpu_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int spmm_multigpu_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, int32_t num_gpus,
+                      int32_t warmup, int32_t iters, float* time_ms, int32_t* used_gpus, int32_t* rows_out,
+                      int32_t* nnz_out, float* bcast_ms) {
+    if (!check_host_view(hA) || N < 0 || warmup < 0 || iters < 1 || !time_ms) return SPMM_ERR_INVALID_ARG;
+    const int visible = spmm_gpu_count();
+    if (visible < 1) return SPMM_ERR_UNSUPPORTED;
+    int G = std::max(1, std::min(num_gpus, visible));
+    std::vector<int32_t> bounds(G + 1);
+    SPMM_TRY(spmm_nnz_balanced_bounds(hA->row_ptr, hA->rows, hA->nnz, G, bounds.data()));
+    const size_t K = hA->cols;
+    const size_t b_elems = K * static_cast<size_t>(N);
+
+    struct Rank {
+        int dev = 0;
+        cudaStream_t s = nullptr;
+        float* dB = nullptr;
+        float* dC = nullptr;
+        void* ws = nullptr;
+        size_t ws_bytes = 0;
+        DeviceCsr A;
+        spmm_csr_host slice{};
+        float ms = 0.f;
+        int rc = SPMM_OK;
+    };
+    std::vector<Rank> ranks(G);
+    int rc = SPMM_OK;
+
+    // Set-up: per-device slice upload and buffers (outside the timing, as in the reference).
+    for (int g = 0; g < G && rc == SPMM_OK; ++g) {
+        Rank& R = ranks[g];
+        R.dev = g;
+        if (cudaSetDevice(g) != cudaSuccess || cudaStreamCreateWithFlags(&R.s, cudaStreamNonBlocking) != cudaSuccess) {
+            rc = SPMM_ERR_CUDA;
+            break;
+        }
+        rc = spmm_csr_row_slice_host(hA, bounds[g], bounds[g + 1], &R.slice);
+        if (rc != SPMM_OK) break;
+        spmm_csr_view sv{R.slice.rows, R.slice.cols, R.slice.nnz, R.slice.row_ptr, R.slice.col_idx, R.slice.values};
+        rc = upload_csr(&sv, &R.A, R.s);
+        if (rc != SPMM_OK) break;
+        if (cudaMalloc(&R.dB, sizeof(float) * std::max<size_t>(b_elems, 1)) != cudaSuccess ||
+            cudaMalloc(&R.dC, sizeof(float) * std::max<size_t>(static_cast<size_t>(sv.rows) * N, 1)) != cudaSuccess) {
+            rc = SPMM_ERR_NO_MEMORY;
+            break;
+        }
+        DeviceState* st = nullptr;
+        rc = device_state(g, &st);
+        if (rc != SPMM_OK) break;
+        rc = csr_f32_workspace_bytes(&sv, N, SPMM_CSR_AUTO, nullptr, st->sm_count, &R.ws_bytes);
+        if (rc != SPMM_OK) break;
+        if (R.ws_bytes) {
+            if (cudaMalloc(&R.ws, R.ws_bytes) != cudaSuccess) {
+                rc = SPMM_ERR_NO_MEMORY;
+                break;
+            }
+            cudaMemsetAsync(R.ws, 0, R.ws_bytes, R.s);
+        }
+    }
+
+    // B: one host->device copy to device 0, then an NCCL broadcast over NVLink.
+    float bcast = 0.f;
+    if (rc == SPMM_OK && b_elems) {
+        cudaSetDevice(0);
+        if (cudaMemcpyAsync(ranks[0].dB, hB, sizeof(float) * b_elems, cudaMemcpyHostToDevice, ranks[0].s) != cudaSuccess ||
+            cudaStreamSynchronize(ranks[0].s) != cudaSuccess)
+            rc = SPMM_ERR_CUDA;
+        if (rc == SPMM_OK && G > 1) {
+            const NcclApi& nc = nccl();
+            std::vector<ncclComm_t> comms(G);
+            std::vector<int> devs(G);
+            for (int g = 0; g < G; ++g) devs[g] = g;
+            if (!nc.ok || nc.comm_init_all(comms.data(), G, devs.data()) != ncclSuccess) {
+                rc = SPMM_ERR_NCCL;
+            } else {
+                cudaEvent_t e0, e1;
+                cudaSetDevice(0);
+                cudaEventCreate(&e0);
+                cudaEventCreate(&e1);
+                cudaEventRecord(e0, ranks[0].s);
+                bool ok = nc.group_start() == ncclSuccess;
+                for (int g = 0; g < G && ok; ++g) {
+                    cudaSetDevice(g);
+                    // The send buffer is read on the root only.
+                    ok = nc.broadcast(ranks[g].dB, ranks[g].dB, b_elems, ncclFloat, 0, comms[g], ranks[g].s) == ncclSuccess;
+                }
+                ok = (nc.group_end() == ncclSuccess) && ok;
+                cudaSetDevice(0);
+                cudaEventRecord(e1, ranks[0].s);
+                for (int g = 0; g < G; ++g) {
+                    cudaSetDevice(g);
+                    if (cudaStreamSynchronize(ranks[g].s) != cudaSuccess) ok = false;
+                }
+                cudaSetDevice(0);
+                cudaEventElapsedTime(&bcast, e0, e1);
+                cudaEventDestroy(e0);
+                cudaEventDestroy(e1);
+                for (int g = 0; g < G; ++g) nc.comm_destroy(comms[g]);
+                if (!ok) rc = SPMM_ERR_NCCL;
+            }
+        }
+    }
+
+    // One host thread per device: warm-up, timed launches, gather of the row slice.
+    if (rc == SPMM_OK) {
+        std::vector<std::thread> pool;
+        for (int g = 0; g < G; ++g) {
+            pool.emplace_back([&, g] {
+                Rank& R = ranks[g];
+                if (cudaSetDevice(g) != cudaSuccess) {
+                    R.rc = SPMM_ERR_CUDA;
+                    return;
+                }
+                DeviceState* st = nullptr;
+                R.rc = device_state(g, &st);
+                if (R.rc != SPMM_OK) return;
+                if (R.A.view.rows > 0) {
+                    R.rc = time_launches(
+                        [&] {
+                            return csr_f32_launch(&R.A.view, R.dB, R.dC, N, SPMM_CSR_AUTO, nullptr, R.ws, R.ws_bytes,
+                                                  R.s, st);
+                        },
+                        warmup, iters, R.s, &R.ms);
+                    if (R.rc == SPMM_OK &&
+                        cudaMemcpyAsync(hC + static_cast<size_t>(bounds[g]) * N, R.dC,
+                                        sizeof(float) * static_cast<size_t>(R.A.view.rows) * N, cudaMemcpyDeviceToHost,
+                                        R.s) != cudaSuccess)
+                        R.rc = SPMM_ERR_CUDA;
+                    if (R.rc == SPMM_OK && cudaStreamSynchronize(R.s) != cudaSuccess) R.rc = SPMM_ERR_CUDA;
+                }
+            });
+        }
+        for (auto& t : pool) t.join();
+        for (int g = 0; g < G; ++g)
+            if (ranks[g].rc != SPMM_OK && rc == SPMM_OK) rc = ranks[g].rc;
+    }
+
+    float worst = 0.f;
+    for (int g = 0; g < G; ++g) {
+        Rank& R = ranks[g];
+        worst = std::max(worst, R.ms);
+        if (rows_out) rows_out[g] = bounds[g + 1] - bounds[g];
+        if (nnz_out) nnz_out[g] = R.slice.nnz;
+        cudaSetDevice(g);
+        if (R.s) cudaStreamSynchronize(R.s);
+        cudaFree(R.dB);
+        cudaFree(R.dC);
+        cudaFree(R.ws);
+        if (R.s) cudaStreamDestroy(R.s);
+        spmm_csr_host_free(&R.slice);
+    }
+    cudaSetDevice(0);
+    *time_ms = worst;
+    if (used_gpus) *used_gpus = G;
+    if (bcast_ms) *bcast_ms = bcast;
+    return rc;
+}
+
+int spmm_unified_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, int32_t warmup, int32_t iters,
+                     float* ms) {
+    if (!check_host_view(hA) || N < 0 || warmup < 0 || iters < 1 || !ms) return SPMM_ERR_INVALID_ARG;
+    DeviceState* st = nullptr;
+    SPMM_TRY(current_device_state(&st));
+    const size_t M = hA->rows, K = hA->cols, nnz = hA->nnz;
+    int* rp = nullptr;
+    int* ci = nullptr;
+    float* v = nullptr;
+    float* B = nullptr;
+    float* C = nullptr;
+    void* ws = nullptr;
+    int rc = SPMM_OK;
+    cudaStream_t s = nullptr;
+    do {
+        if (cudaMallocManaged(&rp, sizeof(int) * (M + 1)) != cudaSuccess ||
+            cudaMallocManaged(&ci, sizeof(int) * std::max<size_t>(nnz, 1)) != cudaSuccess ||
+            cudaMallocManaged(&v, sizeof(float) * std::max<size_t>(nnz, 1)) != cudaSuccess ||
+            cudaMallocManaged(&B, sizeof(float) * std::max<size_t>(K * N, 1)) != cudaSuccess ||
+            cudaMallocManaged(&C, sizeof(float) * std::max<size_t>(M * N, 1)) != cudaSuccess) {
+            rc = SPMM_ERR_NO_MEMORY;
+            break;
+        }
+        std::memcpy(rp, hA->row_ptr, sizeof(int) * (M + 1));
+        if (nnz) {
+            std::memcpy(ci, hA->col_idx, sizeof(int) * nnz);
+            std::memcpy(v, hA->values, sizeof(float) * nnz);
+        }
+        if (K * N != 0) std::memcpy(B, hB, sizeof(float) * K * N);
+        if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
+            rc = SPMM_ERR_CUDA;
+            break;
+        }
+        // Prefetch the working set; platforms without prefetch keep demand paging.
+        cudaMemPrefetchAsync(rp, sizeof(int) * (M + 1), st->device, s);
+        cudaMemPrefetchAsync(ci, sizeof(int) * std::max<size_t>(nnz, 1), st->device, s);
+        cudaMemPrefetchAsync(v, sizeof(float) * std::max<size_t>(nnz, 1), st->device, s);
+        cudaMemPrefetchAsync(B, sizeof(float) * std::max<size_t>(K * N, 1), st->device, s);
+        cudaMemPrefetchAsync(C, sizeof(float) * std::max<size_t>(M * N, 1), st->device, s);
+        cudaGetLastError();
+        spmm_csr_view d = *hA;
+        d.row_ptr = rp;
+        d.col_idx = ci;
+        d.values = v;
+        size_t need = 0;
+        rc = csr_f32_workspace_bytes(&d, N, SPMM_CSR_AUTO, nullptr, st->sm_count, &need);
+        if (rc != SPMM_OK) break;
+        if (need) {
+            if (cudaMalloc(&ws, need) != cudaSuccess) {
+                rc = SPMM_ERR_NO_MEMORY;
+                break;
+            }
+            cudaMemsetAsync(ws, 0, need, s);
+        }
+        rc = time_launches([&] { return csr_f32_launch(&d, B, C, N, SPMM_CSR_AUTO, nullptr, ws, need, s, st); },
+                           warmup, iters, s, ms);
+        if (rc == SPMM_OK && cudaStreamSynchronize(s) != cudaSuccess) rc = SPMM_ERR_CUDA;
+        if (rc == SPMM_OK && M * N != 0) std::memcpy(hC, C, sizeof(float) * M * N);
+    } while (false);
+    if (s) {
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+    }
+    cudaFree(rp);
+    cudaFree(ci);
+    cudaFree(v);
+    cudaFree(B);
+    cudaFree(C);
+    cudaFree(ws);
+    return rc;
+}
+
+}  // extern "C"

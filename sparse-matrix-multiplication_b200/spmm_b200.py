@@ -1,0 +1,395 @@
+"""Python binding of the B200 SpMM engine's C ABI (include/spmm_c.h, lib/libspmm_b200.so).
+
+ctypes only: device buffers are passed as raw pointers (torch tensors are accepted and must
+live on the current CUDA device), host buffers as numpy arrays. There is no fallback: if the
+shared library is missing or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "lib" / "libspmm_b200.so"
+CXX_LIB_PATH = HERE / "lib" / "libspmm.so"
+
+OK = 0
+ERR = {
+    -1: "SPMM_ERR_INVALID_ARG", -2: "SPMM_ERR_MISALIGNED", -3: "SPMM_ERR_CUDA", -4: "SPMM_ERR_NCCL",
+    -5: "SPMM_ERR_TIMEOUT", -6: "SPMM_ERR_UNSUPPORTED", -7: "SPMM_ERR_NO_MEMORY", -8: "SPMM_ERR_BAD_INDEX",
+    -9: "SPMM_ERR_IO", -10: "SPMM_ERR_TOO_LARGE",
+}
+CSR_AUTO, CSR_ROWWARP, CSR_MERGE = 0, 1, 2
+DTYPE_F16, DTYPE_BF16 = 0, 1
+BACKEND_CSR, BACKEND_TC = 0, 1
+
+# Every symbol include/spmm_c.h declares (checked by the CPU test suite).
+EXPORTS = [
+    "spmm_status_string", "spmm_version", "spmm_csr_host_alloc", "spmm_csr_host_free", "spmm_csr_from_coo_host",
+    "spmm_generate_uniform_csr", "spmm_generate_dense", "spmm_csr_row_slice_host", "spmm_csr_read_binary",
+    "spmm_csr_write_binary", "spmm_csr_validate_host", "spmm_csr_to_bsr16_host", "spmm_bsr_host_free",
+    "spmm_bsr_compute_stats", "spmm_nnz_balanced_bounds", "spmm_csr_f32", "spmm_csr_f32_workspace_size",
+    "spmm_csr_f32_ws", "spmm_csr_f32_chunk", "spmm_csr_f32_host", "spmm_convert_f32", "spmm_bsr16",
+    "spmm_bsr16_algo", "spmm_device_error", "spmm_hybrid_default_threshold", "spmm_hybrid_choose",
+    "spmm_backend_name", "spmm_hybrid_run", "spmm_gpu_count", "spmm_multigpu_run", "spmm_unified_run",
+]
+
+
+class SpmmError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {ERR.get(status, status)} ({status_string(status)})")
+
+
+class CsrView(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("nnz", C.c_int32), ("row_ptr", C.c_void_p),
+                ("col_idx", C.c_void_p), ("values", C.c_void_p)]
+
+
+class CsrHost(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("nnz", C.c_int32), ("row_ptr", C.POINTER(C.c_int32)),
+                ("col_idx", C.POINTER(C.c_int32)), ("values", C.POINTER(C.c_float))]
+
+
+class BsrView(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("block_rows", C.c_int32), ("block_cols", C.c_int32),
+                ("num_blocks", C.c_int32), ("nnz", C.c_int32), ("row_ptr", C.c_void_p), ("col_idx", C.c_void_p),
+                ("values", C.c_void_p), ("dtype", C.c_int32)]
+
+
+class BsrHost(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("block_rows", C.c_int32), ("block_cols", C.c_int32),
+                ("num_blocks", C.c_int32), ("nnz", C.c_int32), ("dtype", C.c_int32),
+                ("row_ptr", C.POINTER(C.c_int32)), ("col_idx", C.POINTER(C.c_int32)),
+                ("values", C.POINTER(C.c_uint16))]
+
+
+class BsrStats(C.Structure):
+    _fields_ = [("num_blocks", C.c_int32), ("stored_elements", C.c_int64), ("original_nnz", C.c_int32),
+                ("fill_in_ratio", C.c_double), ("block_density", C.c_double)]
+
+
+class CsrTuning(C.Structure):
+    _fields_ = [("chunk", C.c_int32), ("col_pass", C.c_int32), ("reserved", C.c_int32 * 6)]
+
+
+class HybridPlan(C.Structure):
+    _fields_ = [("backend", C.c_int32), ("fill_in_ratio", C.c_double), ("block_density", C.c_double),
+                ("threshold", C.c_float), ("n_aligned", C.c_int32), ("reason", C.c_char_p)]
+
+
+_lib: C.CDLL | None = None
+
+
+def lib() -> C.CDLL:
+    """Load lib/libspmm_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` (or __graft_entry__.build())")
+    L = C.CDLL(str(LIB_PATH))
+    vp, i32, i64, f32 = C.c_void_p, C.c_int32, C.c_int64, C.c_float
+    sig = {
+        "spmm_status_string": (C.c_char_p, [C.c_int]),
+        "spmm_version": (C.c_int, []),
+        "spmm_csr_host_alloc": (C.c_int, [i32, i32, i32, C.POINTER(CsrHost)]),
+        "spmm_csr_host_free": (None, [C.POINTER(CsrHost)]),
+        "spmm_csr_from_coo_host": (C.c_int, [i32, i32, i32, vp, vp, vp, C.POINTER(CsrHost)]),
+        "spmm_generate_uniform_csr": (C.c_int, [i32, i32, f32, i32, C.POINTER(CsrHost)]),
+        "spmm_generate_dense": (C.c_int, [i32, i32, i32, vp]),
+        "spmm_csr_row_slice_host": (C.c_int, [C.POINTER(CsrView), i32, i32, C.POINTER(CsrHost)]),
+        "spmm_csr_read_binary": (C.c_int, [C.c_char_p, C.POINTER(CsrHost)]),
+        "spmm_csr_write_binary": (C.c_int, [C.POINTER(CsrView), C.c_char_p]),
+        "spmm_csr_validate_host": (C.c_int, [C.POINTER(CsrView), C.POINTER(i32)]),
+        "spmm_csr_to_bsr16_host": (C.c_int, [C.POINTER(CsrView), i32, C.POINTER(BsrHost)]),
+        "spmm_bsr_host_free": (None, [C.POINTER(BsrHost)]),
+        "spmm_bsr_compute_stats": (C.c_int, [C.POINTER(BsrView), C.POINTER(BsrStats)]),
+        "spmm_nnz_balanced_bounds": (C.c_int, [vp, i32, i64, i32, vp]),
+        "spmm_csr_f32": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, vp]),
+        "spmm_csr_f32_workspace_size": (C.c_int, [C.POINTER(CsrView), i32, i32, C.POINTER(CsrTuning),
+                                                   C.POINTER(C.c_size_t)]),
+        "spmm_csr_f32_ws": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, C.POINTER(CsrTuning), vp, C.c_size_t,
+                                      vp]),
+        "spmm_csr_f32_chunk": (C.c_int, [C.POINTER(CsrView), i32, i32, C.POINTER(CsrTuning), C.POINTER(i32)]),
+        "spmm_csr_f32_host": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, vp]),
+        "spmm_convert_f32": (C.c_int, [vp, vp, i64, i32, vp]),
+        "spmm_bsr16": (C.c_int, [C.POINTER(BsrView), vp, vp, i32, vp]),
+        "spmm_bsr16_algo": (C.c_int, [C.POINTER(BsrView), vp, vp, i32, i32, vp]),
+        "spmm_device_error": (C.c_int, [i32, C.POINTER(i32), C.POINTER(i64), i32]),
+        "spmm_hybrid_default_threshold": (f32, []),
+        "spmm_hybrid_choose": (C.c_int, [C.POINTER(CsrView), i32, f32, C.POINTER(HybridPlan)]),
+        "spmm_backend_name": (C.c_char_p, [i32]),
+        "spmm_hybrid_run": (C.c_int, [C.POINTER(HybridPlan), C.POINTER(CsrView), vp, vp, i32, i32, i32,
+                                      C.POINTER(f32)]),
+        "spmm_gpu_count": (C.c_int, []),
+        "spmm_multigpu_run": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, i32, i32, C.POINTER(f32),
+                                        C.POINTER(i32), vp, vp, C.POINTER(f32)]),
+        "spmm_unified_run": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, i32, C.POINTER(f32)]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def status_string(status: int) -> str:
+    try:
+        return lib().spmm_status_string(status).decode()
+    except Exception:  # noqa: BLE001 - used while formatting another error
+        return "?"
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        raise SpmmError(status, what)
+
+
+# ------------------------------------------------------------------ pointers
+
+
+def ptr(x) -> int:
+    """Raw address of a torch tensor or numpy array (0 for None)."""
+    if x is None:
+        return 0
+    if hasattr(x, "data_ptr"):
+        return int(x.data_ptr())
+    return int(x.ctypes.data)
+
+
+def stream_ptr(stream) -> int:
+    if stream is None:
+        return 0
+    if hasattr(stream, "cuda_stream"):
+        return int(stream.cuda_stream)
+    return int(stream)
+
+
+# ------------------------------------------------------------------ host CSR
+
+
+@dataclass
+class HostCSR:
+    rows: int
+    cols: int
+    row_ptr: np.ndarray
+    col_idx: np.ndarray
+    values: np.ndarray
+
+    @property
+    def nnz(self) -> int:
+        return int(self.col_idx.size)
+
+    def view(self) -> CsrView:
+        return CsrView(self.rows, self.cols, self.nnz, ptr(self.row_ptr), ptr(self.col_idx), ptr(self.values))
+
+
+def _adopt(h: CsrHost) -> HostCSR:
+    L = lib()
+    rp = np.ctypeslib.as_array(h.row_ptr, shape=(h.rows + 1,)).copy()
+    ci = np.ctypeslib.as_array(h.col_idx, shape=(h.nnz,)).copy() if h.nnz else np.zeros(0, np.int32)
+    v = np.ctypeslib.as_array(h.values, shape=(h.nnz,)).copy() if h.nnz else np.zeros(0, np.float32)
+    out = HostCSR(h.rows, h.cols, rp, ci, v)
+    L.spmm_csr_host_free(C.byref(h))
+    return out
+
+
+def generate_uniform_csr(rows: int, cols: int, density: float, seed: int) -> HostCSR:
+    h = CsrHost()
+    check(lib().spmm_generate_uniform_csr(rows, cols, density, seed, C.byref(h)), "spmm_generate_uniform_csr")
+    return _adopt(h)
+
+
+def generate_dense(rows: int, cols: int, seed: int) -> np.ndarray:
+    out = np.empty((rows, cols), dtype=np.float32)
+    check(lib().spmm_generate_dense(rows, cols, seed, ptr(out)), "spmm_generate_dense")
+    return out
+
+
+def csr_from_coo(rows: int, cols: int, r, c, v) -> HostCSR:
+    r = np.ascontiguousarray(r, np.int32)
+    c = np.ascontiguousarray(c, np.int32)
+    v = np.ascontiguousarray(v, np.float32)
+    h = CsrHost()
+    check(lib().spmm_csr_from_coo_host(rows, cols, int(v.size), ptr(r), ptr(c), ptr(v), C.byref(h)),
+          "spmm_csr_from_coo_host")
+    return _adopt(h)
+
+
+def row_slice(A: HostCSR, b: int, e: int) -> HostCSR:
+    h = CsrHost()
+    v = A.view()
+    check(lib().spmm_csr_row_slice_host(C.byref(v), b, e, C.byref(h)), "spmm_csr_row_slice_host")
+    return _adopt(h)
+
+
+def read_binary(path: str | os.PathLike) -> HostCSR:
+    h = CsrHost()
+    check(lib().spmm_csr_read_binary(os.fsencode(path), C.byref(h)), "spmm_csr_read_binary")
+    return _adopt(h)
+
+
+def write_binary(A: HostCSR, path: str | os.PathLike) -> None:
+    v = A.view()
+    check(lib().spmm_csr_write_binary(C.byref(v), os.fsencode(path)), "spmm_csr_write_binary")
+
+
+def validate(A: HostCSR) -> int:
+    """-1 when A is well formed, else the first bad row (raises on bad arguments)."""
+    bad = C.c_int32(-1)
+    v = A.view()
+    rc = lib().spmm_csr_validate_host(C.byref(v), C.byref(bad))
+    if rc == OK:
+        return -1
+    if bad.value >= 0:
+        return bad.value
+    raise SpmmError(rc, "spmm_csr_validate_host")
+
+
+@dataclass
+class HostBSR:
+    rows: int
+    cols: int
+    block_rows: int
+    block_cols: int
+    row_ptr: np.ndarray
+    col_idx: np.ndarray
+    values: np.ndarray  # uint16 bits
+    nnz: int
+    dtype: int
+
+    @property
+    def num_blocks(self) -> int:
+        return int(self.col_idx.size)
+
+    def view(self) -> BsrView:
+        return BsrView(self.rows, self.cols, self.block_rows, self.block_cols, self.num_blocks, self.nnz,
+                       ptr(self.row_ptr), ptr(self.col_idx), ptr(self.values), self.dtype)
+
+
+def csr_to_bsr16(A: HostCSR, dtype: int = DTYPE_F16) -> HostBSR:
+    b = BsrHost()
+    v = A.view()
+    check(lib().spmm_csr_to_bsr16_host(C.byref(v), dtype, C.byref(b)), "spmm_csr_to_bsr16_host")
+    nb = b.num_blocks
+    out = HostBSR(b.rows, b.cols, b.block_rows, b.block_cols,
+                  np.ctypeslib.as_array(b.row_ptr, shape=(b.block_rows + 1,)).copy(),
+                  np.ctypeslib.as_array(b.col_idx, shape=(nb,)).copy() if nb else np.zeros(0, np.int32),
+                  np.ctypeslib.as_array(b.values, shape=(nb * 256,)).copy() if nb else np.zeros(0, np.uint16),
+                  b.nnz, b.dtype)
+    lib().spmm_bsr_host_free(C.byref(b))
+    return out
+
+
+def bsr_stats(B: HostBSR) -> dict:
+    s = BsrStats()
+    v = B.view()
+    check(lib().spmm_bsr_compute_stats(C.byref(v), C.byref(s)), "spmm_bsr_compute_stats")
+    return {"num_blocks": s.num_blocks, "stored_elements": s.stored_elements, "original_nnz": s.original_nnz,
+            "fill_in_ratio": s.fill_in_ratio, "block_density": s.block_density}
+
+
+def nnz_balanced_bounds(row_ptr: np.ndarray, rows: int, nnz: int, G: int) -> np.ndarray:
+    row_ptr = np.ascontiguousarray(row_ptr, np.int32)
+    out = np.zeros(G + 1, dtype=np.int32)
+    check(lib().spmm_nnz_balanced_bounds(ptr(row_ptr), rows, nnz, G, ptr(out)), "spmm_nnz_balanced_bounds")
+    return out
+
+
+def hybrid_choose(A: HostCSR, N: int, threshold: float = 0.0) -> dict:
+    p = HybridPlan()
+    v = A.view()
+    check(lib().spmm_hybrid_choose(C.byref(v), N, threshold, C.byref(p)), "spmm_hybrid_choose")
+    return {"backend": p.backend, "backend_name": lib().spmm_backend_name(p.backend).decode(),
+            "fill_in_ratio": p.fill_in_ratio, "block_density": p.block_density, "threshold": p.threshold,
+            "n_aligned": bool(p.n_aligned), "reason": p.reason.decode(), "_plan": p}
+
+
+# ------------------------------------------------------------------ device compute
+
+
+def device_view(rows: int, cols: int, row_ptr, col_idx, values) -> CsrView:
+    """CsrView over device tensors (int32 row_ptr/col_idx, float32 values)."""
+    nnz = int(col_idx.numel()) if hasattr(col_idx, "numel") else int(col_idx.size)
+    return CsrView(rows, cols, nnz, ptr(row_ptr), ptr(col_idx), ptr(values))
+
+
+def csr_f32(A: CsrView, B, Cout, N: int, algo: int = CSR_AUTO, stream=None) -> None:
+    check(lib().spmm_csr_f32(C.byref(A), ptr(B), ptr(Cout), N, algo, stream_ptr(stream)), "spmm_csr_f32")
+
+
+def csr_f32_ws(A: CsrView, B, Cout, N: int, algo: int, tuning: CsrTuning | None, ws, ws_bytes: int,
+               stream=None) -> None:
+    t = C.byref(tuning) if tuning is not None else None
+    check(lib().spmm_csr_f32_ws(C.byref(A), ptr(B), ptr(Cout), N, algo, t, ptr(ws), ws_bytes, stream_ptr(stream)),
+          "spmm_csr_f32_ws")
+
+
+def csr_workspace_size(A: CsrView, N: int, algo: int = CSR_AUTO, tuning: CsrTuning | None = None) -> int:
+    n = C.c_size_t()
+    t = C.byref(tuning) if tuning is not None else None
+    check(lib().spmm_csr_f32_workspace_size(C.byref(A), N, algo, t, C.byref(n)), "spmm_csr_f32_workspace_size")
+    return int(n.value)
+
+
+def csr_chunk(A: CsrView, N: int, algo: int = CSR_AUTO, tuning: CsrTuning | None = None) -> int:
+    c = C.c_int32()
+    t = C.byref(tuning) if tuning is not None else None
+    check(lib().spmm_csr_f32_chunk(C.byref(A), N, algo, t, C.byref(c)), "spmm_csr_f32_chunk")
+    return int(c.value)
+
+
+def csr_f32_host(A: HostCSR, B: np.ndarray, Cout: np.ndarray, N: int, algo: int = CSR_AUTO, stream=None) -> None:
+    v = A.view()
+    check(lib().spmm_csr_f32_host(C.byref(v), ptr(B), ptr(Cout), N, algo, stream_ptr(stream)), "spmm_csr_f32_host")
+
+
+def convert_f32(src, dst, n: int, dtype: int = DTYPE_F16, stream=None) -> None:
+    check(lib().spmm_convert_f32(ptr(src), ptr(dst), n, dtype, stream_ptr(stream)), "spmm_convert_f32")
+
+
+def bsr16(A: BsrView, B16, Cout, N: int, algo: int = 0, stream=None) -> None:
+    check(lib().spmm_bsr16_algo(C.byref(A), ptr(B16), ptr(Cout), N, algo, stream_ptr(stream)), "spmm_bsr16")
+
+
+def device_error(device: int = 0, clear: bool = True) -> tuple[int, int]:
+    code, detail = C.c_int32(), C.c_int64()
+    check(lib().spmm_device_error(device, C.byref(code), C.byref(detail), int(clear)), "spmm_device_error")
+    return int(code.value), int(detail.value)
+
+
+def gpu_count() -> int:
+    return int(lib().spmm_gpu_count())
+
+
+def hybrid_run(plan: dict, A: HostCSR, B: np.ndarray, Cout: np.ndarray, N: int, warmup: int, iters: int) -> float:
+    ms = C.c_float()
+    v = A.view()
+    check(lib().spmm_hybrid_run(C.byref(plan["_plan"]), C.byref(v), ptr(B), ptr(Cout), N, warmup, iters,
+                                C.byref(ms)), "spmm_hybrid_run")
+    return float(ms.value)
+
+
+def multigpu_run(A: HostCSR, B: np.ndarray, Cout: np.ndarray, N: int, gpus: int, warmup: int, iters: int) -> dict:
+    ms, used, bc = C.c_float(), C.c_int32(), C.c_float()
+    rows = np.zeros(max(gpus, 1), np.int32)
+    nnz = np.zeros(max(gpus, 1), np.int32)
+    v = A.view()
+    check(lib().spmm_multigpu_run(C.byref(v), ptr(B), ptr(Cout), N, gpus, warmup, iters, C.byref(ms), C.byref(used),
+                                  ptr(rows), ptr(nnz), C.byref(bc)), "spmm_multigpu_run")
+    g = int(used.value)
+    return {"time_ms": float(ms.value), "num_gpus": g, "rows": rows[:g].tolist(), "nnz": nnz[:g].tolist(),
+            "bcast_ms": float(bc.value)}
+
+
+def unified_run(A: HostCSR, B: np.ndarray, Cout: np.ndarray, N: int, warmup: int, iters: int) -> float:
+    ms = C.c_float()
+    v = A.view()
+    check(lib().spmm_unified_run(C.byref(v), ptr(B), ptr(Cout), N, warmup, iters, C.byref(ms)), "spmm_unified_run")
+    return float(ms.value)

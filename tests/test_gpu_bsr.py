@@ -1,0 +1,117 @@
+"""GPU parity of the BSR-16 tensor-core path (tcgen05) and the FP32 -> FP16/BF16 conversion.
+
+Tolerances (BASELINE: "FP16/BF16 BSR output within 1e-2 relative to an FP32 result"):
+  * against the FP64 oracle on the same 16-bit-rounded inputs (the arithmetic the tensor
+    cores are asked to do): max |err| / max |ref| <= 1e-5 and compare()'s filtered max
+    relative error <= 1e-3 -- products are exact, only the FP32 accumulation rounds;
+  * against the FP32 CSR result on the unrounded inputs: rel_l2 <= 1e-2.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import _cases as K
+import spmm_b200 as S
+from oracle import oracle as O
+from oracle import patterns as P
+
+pytestmark = pytest.mark.gpu
+
+
+def run_bsr(torch, Hb: S.HostBSR, B16: np.ndarray, N: int, algo: int = 0, c_off: int = 0):
+    dev = torch.device("cuda")
+    brp = torch.from_numpy(Hb.row_ptr).to(dev)
+    bci = torch.from_numpy(Hb.col_idx).to(dev)
+    bva = torch.from_numpy(Hb.values.view(np.int16)).to(dev)
+    Bt = torch.from_numpy(np.ascontiguousarray(B16).view(np.int16)).to(dev)
+    Cbuf = torch.full((Hb.rows * N + c_off + 4,), float("nan"), dtype=torch.float32, device=dev)
+    view = Hb.view()
+    view.row_ptr, view.col_idx, view.values = S.ptr(brp), S.ptr(bci), S.ptr(bva)
+    S.bsr16(view, Bt, Cbuf[c_off:], N, algo, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    code, detail = S.device_error(0)
+    assert code == 0, f"device error {code} ({detail})"
+    return Cbuf[c_off:c_off + Hb.rows * N].view(Hb.rows, N).cpu().numpy()
+
+
+def check_bsr(got: np.ndarray, Hb: S.HostBSR, B16: np.ndarray, dtype: int):
+    ob = O.BSR(Hb.rows, Hb.cols, Hb.block_rows, Hb.block_cols, Hb.row_ptr, Hb.col_idx, Hb.values, Hb.nnz)
+    ref = O.spmm_bsr_f64(ob, B16, dtype)
+    scale = max(float(np.abs(ref).max()), 1e-30)
+    assert float(np.abs(got - ref).max()) / scale <= 1e-5
+    _, max_rel, _ = O.compare(got, ref.astype(np.float32))
+    assert max_rel <= 1e-3
+    return ref
+
+
+@pytest.mark.parametrize("dtype", [S.DTYPE_F16, S.DTYPE_BF16])
+def test_config3_block_diagonal(cuda, dtype):
+    A, Bf = K.config("c3")
+    Hb = S.csr_to_bsr16(A, dtype)
+    st = S.bsr_stats(Hb)
+    assert st["num_blocks"] == 4096 and st["fill_in_ratio"] == 1.0
+    B16 = O.to_half_bits(Bf, bf16=dtype == S.DTYPE_BF16)
+    got = run_bsr(cuda, Hb, B16, 256, algo=1)
+    check_bsr(got, Hb, B16, dtype)
+    # Against the FP32 CSR product of the unrounded inputs.
+    c32 = O.spmm_csr_f32(K.to_oracle(A), Bf)
+    assert np.linalg.norm(got - c32) / np.linalg.norm(c32) <= 1e-2
+
+
+@pytest.mark.parametrize("algo", [1, 2])
+def test_config2_banded(cuda, algo):
+    A, Bf = K.config("c2")
+    Hb = S.csr_to_bsr16(A)
+    assert Hb.num_blocks == 3572
+    B16 = O.to_half_bits(Bf)
+    check_bsr(run_bsr(cuda, Hb, B16, 128, algo=algo), Hb, B16, S.DTYPE_F16)
+
+
+@pytest.mark.parametrize("M,Kc,N", [(16, 16, 8), (33, 47, 24), (100, 70, 136), (1000, 999, 128), (257, 4096, 256),
+                                    (2048, 512, 40)])
+@pytest.mark.parametrize("algo", [1, 2])
+def test_ragged_shapes(cuda, M, Kc, N, algo):
+    A = K.random_csr(M, Kc, np.random.default_rng(M).integers(0, min(Kc, 40), size=M), seed=M + Kc)
+    Hb = S.csr_to_bsr16(A)
+    B16 = O.to_half_bits(K.dense(Kc, N, 3))
+    check_bsr(run_bsr(cuda, Hb, B16, N, algo=algo), Hb, B16, S.DTYPE_F16)
+
+
+def test_empty_block_rows_and_uniform_fill(cuda):
+    # Uniform sparsity (high fill-in) with whole empty block-rows in between.
+    lens = np.random.default_rng(1).integers(0, 30, size=512)
+    lens[64:160] = 0
+    A = K.random_csr(512, 2048, lens, seed=4)
+    Hb = S.csr_to_bsr16(A)
+    B16 = O.to_half_bits(K.dense(2048, 128, 5))
+    for algo in (1, 2):
+        check_bsr(run_bsr(cuda, Hb, B16, 128, algo=algo), Hb, B16, S.DTYPE_F16)
+
+
+def test_unaligned_n_falls_back(cuda):
+    A = K.random_csr(64, 64, np.full(64, 8), seed=1)
+    Hb = S.csr_to_bsr16(A)
+    B16 = O.to_half_bits(K.dense(64, 20, 2))
+    with pytest.raises(S.SpmmError) as e:
+        run_bsr(cuda, Hb, B16, 20, algo=1)  # tensor-core path demands N % 8 == 0
+    assert e.value.status == -2
+    check_bsr(run_bsr(cuda, Hb, B16, 20, algo=0), Hb, B16, S.DTYPE_F16)
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_convert_round_to_nearest_even(cuda, bf16):
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.uniform(-1, 1, 100003).astype(np.float32),
+                        np.array([0.0, -0.0, 65504.0, 65519.99, 65520.0, 1e-8, 5.96e-8, 2.98e-8, 6.1e-5, 1e30, -1e30,
+                                  np.inf, -np.inf, 1.0 + 2**-11, 1.0 + 3 * 2**-11, 3.0e38], np.float32)])
+    torch = cuda
+    src = torch.from_numpy(x).cuda()
+    for off in (0, 1):  # vector and scalar kernels
+        dst = torch.empty(x.size - off, dtype=torch.int16, device="cuda")
+        S.convert_f32(src[off:], dst, x.size - off, S.DTYPE_BF16 if bf16 else S.DTYPE_F16,
+                      torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        got = dst.cpu().numpy().view(np.uint16)
+        want = O.to_half_bits(x[off:], bf16=bf16)
+        assert np.array_equal(got, want)

@@ -1,0 +1,201 @@
+"""GPU parity of the FP32 CSR path (spmm_csr_f32 through the C ABI) against the CPU oracle.
+
+The bar is bit equality: every output element of the engine must equal the oracle's FP32
+arithmetic bit for bit -- the reference's sequential FMA chain per element, with long rows
+(more than `chunk` nonzeros) cut at the documented merge-path boundaries and the pieces added
+left to right (oracle.spmm_csr_f32_split). The FP64 oracle is checked alongside with the
+tolerance BASELINE states for FP32 (rel_l2 <= 1e-5 here; see the per-test comments).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import _cases as K
+import spmm_b200 as S
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def run(torch, A: S.HostCSR, B: np.ndarray, algo=S.CSR_AUTO, tuning=None, b_off=0, c_off=0):
+    """C = A @ B on the GPU; b_off / c_off shift B and C by that many floats (alignment)."""
+    N = B.shape[1]
+    rp, ci, v = _dev(torch, A.row_ptr), _dev(torch, A.col_idx), _dev(torch, A.values)
+    Bbuf = torch.empty(B.size + b_off + 4, dtype=torch.float32, device="cuda")
+    Bbuf[b_off:b_off + B.size].copy_(torch.from_numpy(B.ravel()))
+    Cbuf = torch.full((A.rows * N + c_off + 4,), float("nan"), dtype=torch.float32, device="cuda")
+    view = S.device_view(A.rows, A.cols, rp, ci, v)
+    Bp, Cp = Bbuf[b_off:], Cbuf[c_off:]
+    stream = torch.cuda.current_stream()
+    if tuning is None:
+        S.csr_f32(view, Bp, Cp, N, algo, stream)
+    else:
+        n = S.csr_workspace_size(view, N, algo, tuning)
+        ws = torch.zeros(max(n, 16), dtype=torch.uint8, device="cuda")
+        S.csr_f32_ws(view, Bp, Cp, N, algo, tuning, ws, n, stream)
+        torch.cuda.synchronize()
+        if n:
+            assert _counters_zero(ws, view, N, tuning), "merge-path counters must be back to zero after the call"
+    torch.cuda.synchronize()
+    code, detail = S.device_error(0)
+    assert code == 0, f"device error {code} at {detail}"
+    return Cbuf[c_off:c_off + A.rows * N].view(A.rows, N).cpu().numpy()
+
+
+def _counters_zero(ws, view, N, tuning) -> bool:
+    """The counter block (first num_chunks ints) is zero; partial slots may hold data."""
+    chunk = S.csr_chunk(view, N, S.CSR_MERGE, tuning)
+    chunks = (view.rows + view.nnz + chunk - 1) // chunk
+    return int(ws[: 4 * chunks].count_nonzero()) == 0
+
+
+def chunk_of(A: S.HostCSR, N: int, tuning=None) -> int:
+    return S.csr_chunk(A.view(), N, S.CSR_MERGE, tuning)
+
+
+def expect(A: S.HostCSR, B: np.ndarray, algo=S.CSR_AUTO, tuning=None) -> np.ndarray:
+    oa = K.to_oracle(A)
+    if algo == S.CSR_ROWWARP:
+        return O.spmm_csr_f32(oa, B, dynamic=True)
+    return O.spmm_csr_f32_split(oa, B, chunk_of(A, B.shape[1], tuning))
+
+
+def bits_equal(x: np.ndarray, y: np.ndarray) -> bool:
+    return x.shape == y.shape and np.array_equal(x.view(np.uint32), y.view(np.uint32))
+
+
+def assert_parity(got, A, B, algo=S.CSR_AUTO, tuning=None):
+    want = expect(A, B, algo, tuning)
+    if not bits_equal(got, want):
+        diff = np.argwhere(got.view(np.uint32) != want.view(np.uint32))
+        i, j = diff[0]
+        raise AssertionError(f"{len(diff)} elements differ; first ({i},{j}): got {got[i, j]!r} want {want[i, j]!r}")
+    # Accuracy against FP64 (rel_l2, the reference's own FP32 bar is 1e-4; README.md:237).
+    ref64 = O.spmm_csr_f64(K.to_oracle(A), B)
+    den = np.linalg.norm(ref64)
+    if den > 0:
+        assert np.linalg.norm(got - ref64) / den <= 1e-5
+
+
+@pytest.mark.parametrize("algo", [S.CSR_MERGE, S.CSR_ROWWARP])
+def test_config1_uniform_bit_exact(cuda, algo):
+    A, B = K.config("c1")
+    assert A.nnz == 167686  # README.md:233
+    assert_parity(run(cuda, A, B, algo), A, B, algo)
+
+
+@pytest.mark.parametrize("algo", [S.CSR_MERGE, S.CSR_ROWWARP])
+def test_config2_banded_bit_exact(cuda, algo):
+    A, B = K.config("c2")
+    assert A.nnz == 678214
+    assert_parity(run(cuda, A, B, algo), A, B, algo)
+
+
+@pytest.mark.parametrize("algo", [S.CSR_MERGE, S.CSR_ROWWARP])
+def test_config4_power_law_bit_exact(cuda, algo):
+    A, B = K.config("c4")
+    assert A.nnz == 2686981 and int(np.diff(A.row_ptr).max()) == 14850
+    got = run(cuda, A, B, algo)
+    assert_parity(got, A, B, algo)
+
+
+@pytest.mark.parametrize("chunk", [64, 96, 128, 512, 2048, 8192])
+def test_long_rows_any_chunk(cuda, chunk):
+    # Skewed rows (0 .. 3000 nonzeros) so that rows are cut into 1 .. 47 pieces.
+    rng = np.random.default_rng(7)
+    lens = rng.integers(0, 40, size=700)
+    lens[[3, 100, 101, 350, 699]] = [3000, 1500, 65, 2049, 777]
+    A = K.random_csr(700, 4000, lens, seed=8)
+    B = K.dense(4000, 96, 9)
+    t = S.CsrTuning(chunk=chunk)
+    assert_parity(run(cuda, A, B, S.CSR_MERGE, tuning=t), A, B, S.CSR_MERGE, tuning=t)
+
+
+@pytest.mark.parametrize("N", [1, 2, 3, 8, 16, 31, 32, 33, 48, 64, 96, 100, 128, 160, 255, 256, 257, 384, 512, 1000])
+def test_every_width(cuda, N):
+    A = K.random_csr(300, 500, np.random.default_rng(N).integers(0, 90, size=300), seed=N)
+    B = K.dense(500, N, N + 1)
+    for algo in (S.CSR_MERGE, S.CSR_ROWWARP):
+        assert_parity(run(cuda, A, B, algo), A, B, algo)
+
+
+@pytest.mark.parametrize("b_off,c_off", [(1, 0), (0, 1), (2, 2), (1, 3)])
+def test_misaligned_operands(cuda, b_off, c_off):
+    A = K.random_csr(200, 300, np.random.default_rng(1).integers(0, 50, size=200), seed=2)
+    B = K.dense(300, 128, 3)
+    assert_parity(run(cuda, A, B, S.CSR_MERGE, b_off=b_off, c_off=c_off), A, B)
+
+
+@pytest.mark.parametrize("shape", ["empty_rows", "nnz0", "one_row", "one_col", "single_long_row", "tail_empty"])
+def test_edge_shapes(cuda, shape):
+    if shape == "empty_rows":
+        lens = np.zeros(500, np.int64)
+        lens[::7] = 5
+        A = K.random_csr(500, 64, lens, seed=1)
+    elif shape == "nnz0":
+        A = K.random_csr(100, 50, np.zeros(100, np.int64), seed=1)
+    elif shape == "one_row":
+        A = K.random_csr(1, 1000, [400], seed=1)
+    elif shape == "one_col":
+        A = K.random_csr(300, 1, np.random.default_rng(3).integers(0, 2, size=300), seed=1)
+    elif shape == "single_long_row":
+        lens = np.zeros(64, np.int64)
+        lens[31] = 14850
+        A = K.random_csr(64, 16384, lens, seed=1)
+    else:
+        lens = np.zeros(4000, np.int64)
+        lens[:10] = 300
+        A = K.random_csr(4000, 500, lens, seed=1)
+    B = K.dense(A.cols, 64, 5)
+    for algo in (S.CSR_MERGE, S.CSR_ROWWARP):
+        assert_parity(run(cuda, A, B, algo), A, B, algo)
+
+
+def test_bad_index_is_reported_not_faulted(cuda):
+    A = K.random_csr(64, 100, np.full(64, 10), seed=1)
+    bad = S.HostCSR(A.rows, A.cols, A.row_ptr.copy(), A.col_idx.copy(), A.values.copy())
+    bad.col_idx[5] = A.cols + 7  # out of range: the kernel records it and reads a safe row
+    torch = cuda
+    rp, ci, v = _dev(torch, bad.row_ptr), _dev(torch, bad.col_idx), _dev(torch, bad.values)
+    B = _dev(torch, K.dense(100, 32, 1))
+    Cout = torch.empty(64, 32, device="cuda")
+    S.csr_f32(S.device_view(64, 100, rp, ci, v), B, Cout, 32, S.CSR_AUTO, torch.cuda.current_stream())
+    code, detail = S.device_error(0, clear=True)
+    assert code == -8 and detail == 5
+    # The record is cleared and the next valid call is clean and exact.
+    assert_parity(run(cuda, A, K.dense(100, 32, 1)), A, K.dense(100, 32, 1))
+
+
+def test_host_buffer_entry_point(cuda):
+    A, B = K.config("c1")
+    C = np.empty((A.rows, B.shape[1]), np.float32)
+    S.csr_f32_host(A, B, C, B.shape[1])
+    assert bits_equal(C, expect(A, B))
+    C2 = np.empty_like(C)
+    S.csr_f32_host(A, B, C2, B.shape[1])  # cached device buffers, second call
+    assert bits_equal(C2, C)
+
+
+def test_config5_full_size_properties(cuda):
+    """C5 at its full size (131072^2, ~17.2M nnz, N=256): exact rows on a sample, and a
+    size-independent identity for the whole product, C @ x == A @ (B @ x)."""
+    A, B = K.config("c5")
+    assert abs(A.nnz - 17179869) < 20000
+    got = run(cuda, A, B, S.CSR_AUTO)
+    # No row is long at this size, so every row is the reference's sequential chain.
+    assert int(np.diff(A.row_ptr).max()) <= chunk_of(A, 256)
+    for r0 in (0, 65536 - 512, 131072 - 1024):
+        sl = S.row_slice(A, r0, r0 + 1024)
+        want = O.spmm_csr_f32(K.to_oracle(sl), B)
+        assert bits_equal(got[r0:r0 + 1024], want)
+    x = np.random.default_rng(0).uniform(-1, 1, size=256)
+    lhs = got.astype(np.float64) @ x
+    bx = B.astype(np.float64) @ x
+    rows = np.repeat(np.arange(A.rows), np.diff(A.row_ptr))
+    rhs = np.bincount(rows, weights=A.values.astype(np.float64) * bx[A.col_idx], minlength=A.rows)
+    assert np.linalg.norm(lhs - rhs) / np.linalg.norm(rhs) < 1e-6
