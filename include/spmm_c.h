@@ -178,6 +178,22 @@ int spmm_csr_f32_ws(const spmm_csr_view* A, const float* B, float* C, int32_t N,
 int spmm_csr_f32_chunk(const spmm_csr_view* A, int32_t N, int32_t algo,
                        const spmm_csr_tuning* tune, int32_t* chunk);
 
+/* spmm_csr_f32 for callers that must not allocate device memory (no counterpart in the
+ * reference, whose launchers need no scratch). Hosts that hand all device memory to their
+ * own allocator or a fixed budget, or loops that cannot take cudaMalloc's implicit device
+ * synchronisation, cannot use spmm_csr_f32, which allocates its workspace on first use.
+ * This variant allocates nothing: its scratch is a 16 MiB array compiled into the library
+ * (held by every GPU that loads the library until the process exits). Calls whose workspace
+ * would exceed 16 MiB -- about ((M + nnz) / chunk) * (8 * N + 4) bytes, see
+ * spmm_csr_f32_workspace_size -- return SPMM_ERR_TOO_LARGE. The first call on a device looks
+ * up the array's device address; make it before any stream capture. All calls on a device
+ * share the array, so calls that overlap on the GPU race; the counters that must start at
+ * zero are cleared on `stream` before each launch. Bad indices are replaced by a safe one but
+ * not reported (spmm_device_error does not see this path): validate A beforehand. Same
+ * results as spmm_csr_f32 with the same algo, bit for bit. */
+int spmm_csr_f32_noalloc(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
+                         void* stream);
+
 /* End-to-end call on HOST buffers: copies A and B to the current device (pinned or
  * pageable host memory), computes, copies C back, synchronises `stream`. Device buffers
  * are cached by the library between calls. */

@@ -36,6 +36,7 @@ EXPORTS = [
     "spmm_csr_f32_ws", "spmm_csr_f32_chunk", "spmm_csr_f32_host", "spmm_convert_f32", "spmm_bsr16",
     "spmm_bsr16_algo", "spmm_device_error", "spmm_hybrid_default_threshold", "spmm_hybrid_choose",
     "spmm_backend_name", "spmm_hybrid_run", "spmm_gpu_count", "spmm_multigpu_run", "spmm_unified_run",
+    "spmm_csr_f32_noalloc",
 ]
 
 
@@ -130,6 +131,7 @@ def lib() -> C.CDLL:
         "spmm_multigpu_run": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, i32, i32, C.POINTER(f32),
                                         C.POINTER(i32), vp, vp, C.POINTER(f32)]),
         "spmm_unified_run": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, i32, C.POINTER(f32)]),
+        "spmm_csr_f32_noalloc": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
