@@ -235,6 +235,9 @@ def main():
     torch.cuda.synchronize()
     bcast_ms = 0.0
     if world > 1:
+        warm = torch.zeros(1024, dtype=torch.float32, device=dev)
+        dist.broadcast(warm, src=0)  # communicator set-up stays out of the timed broadcast
+        torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()

@@ -133,6 +133,21 @@ void spmm_bsr_host_free(spmm_bsr_host* b);
 /* (reference: src/bsr.h:79-80, bsr_compute_stats; src/bsr.cu:149-162) */
 int spmm_bsr_compute_stats(const spmm_bsr_view* b, spmm_bsr_stats* out);
 
+/* CSR -> BSR-16 on the GPU, bit-identical to spmm_csr_to_bsr16_host (the reference's
+ * bsr_from_csr_host, src/bsr.cu:30-109, which runs on the host). Device pointers, two steps:
+ *   count: fills d_bsr_row_ptr (block_rows + 1 ints) and returns *num_blocks (synchronises
+ *          `stream`); with num_blocks the fill-in ratio is num_blocks * 256 / nnz.
+ *   fill : writes d_col_idx (num_blocks ints) and d_values (num_blocks * 256 16-bit values,
+ *          4-byte aligned).
+ * Needs columns sorted within each row and K <= 1,048,576 (SPMM_ERR_UNSUPPORTED otherwise:
+ * use the host conversion); an index outside [0, K) gives SPMM_ERR_BAD_INDEX.
+ * (replaces the host-side conversion the reference runs twice per hybrid run,
+ *  src/spmm_hybrid.cu:38,78) */
+int spmm_csr_to_bsr16_device_count(const spmm_csr_view* dA, int32_t* d_bsr_row_ptr, int32_t* num_blocks,
+                                   void* stream);
+int spmm_csr_to_bsr16_device_fill(const spmm_csr_view* dA, const int32_t* d_bsr_row_ptr, int32_t* d_col_idx,
+                                  uint16_t* d_values, int32_t dtype, void* stream);
+
 /* nnz-balanced row partition into G ranges: out[0..G], out[g]..out[g+1] is range g.
  * Bit-identical to the reference's partition. (reference: src/spmm_multigpu.cu:26-40) */
 int spmm_nnz_balanced_bounds(const int32_t* row_ptr, int32_t rows, int64_t nnz, int32_t G,
@@ -146,11 +161,15 @@ int spmm_nnz_balanced_bounds(const int32_t* row_ptr, int32_t rows, int64_t nnz, 
 #define SPMM_CSR_MERGE 2    /* nnz-balanced merge-path chunks; long rows split + fix-up   */
 
 /* Tuning knobs; zero fields take the library default. chunk = merge-path items per warp
- * (a multiple of 32, 64..8192); it also sets the long-row threshold. */
+ * (a multiple of 32, 64..8192); it also sets the long-row threshold. col_pass = width of a
+ * column slab (the grid walks N slab by slab so a slab's B columns stay in L2): 0 = auto,
+ * else 32/64/128/256. b_policy: 0 = B loads carry an L2 evict-last hint, 1 = plain loads,
+ * 2 = evict-last and no L1 allocation. */
 typedef struct spmm_csr_tuning {
     int32_t chunk;
-    int32_t col_pass; /* columns a warp covers per pass: 0 = auto, else 32/64/128/256 */
-    int32_t reserved[6];
+    int32_t col_pass;
+    int32_t b_policy;
+    int32_t reserved[5];
 } spmm_csr_tuning;
 
 /* C = A * B, FP32, on `stream`; A, B, C are device pointers. Asynchronous.
@@ -184,8 +203,8 @@ int spmm_csr_f32_chunk(const spmm_csr_view* A, int32_t N, int32_t algo,
  * synchronisation, cannot use spmm_csr_f32, which allocates its workspace on first use.
  * This variant allocates nothing: its scratch is a 16 MiB array compiled into the library
  * (held by every GPU that loads the library until the process exits). Calls whose workspace
- * would exceed 16 MiB -- about ((M + nnz) / chunk) * (8 * N + 4) bytes, see
- * spmm_csr_f32_workspace_size -- return SPMM_ERR_TOO_LARGE. The first call on a device looks
+ * would exceed 16 MiB -- about ((M + nnz) / chunk) * 8.1 * N bytes, exactly what
+ * spmm_csr_f32_workspace_size reports -- return SPMM_ERR_TOO_LARGE. The first call on a device looks
  * up the array's device address; make it before any stream capture. All calls on a device
  * share the array, so calls that overlap on the GPU race; the counters that must start at
  * zero are cleared on `stream` before each launch. Bad indices are replaced by a safe one but

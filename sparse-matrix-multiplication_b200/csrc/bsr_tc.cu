@@ -18,7 +18,7 @@
 // once (2 boxes of 16 x 64) plus the blocks of the block-rows that contain it, and the MMA
 // warp issues one MMA per such block into that block-row's TMEM columns. So a B tile shared
 // by several block-rows (e.g. dense diagonal blocks larger than 16) crosses L2 once per CTA.
-// A 4-deep shared-memory ring with mbarriers decouples TMA and MMA; four epilogue warps move
+// An 8-deep shared-memory ring with mbarriers decouples TMA and MMA; four epilogue warps move
 // TMEM -> registers -> coalesced FP32 stores.
 //
 // Every mbarrier wait is bounded (iteration count and %globaltimer); on expiry the kernel
@@ -41,7 +41,7 @@
 namespace spmm_b200 {
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kStages = 8;
 constexpr int kColCache = 4096;       // block-column indices cached in shared memory per CTA
 constexpr int kTcThreads = 192;       // warp 0 TMA, warp 1 MMA + TMEM, warps 2..5 epilogue
 constexpr unsigned kFullMask = 0xffffffffu;
@@ -244,6 +244,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == 0) {
         // ---------------- producer: merge G block-column lists, TMA-load tiles
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+        }
         int cur = 0, end = 0;
         if (lane < G) {
             cur = rp[lane];

@@ -57,6 +57,8 @@ struct DeviceState {
     void* h_v = nullptr;  size_t h_v_bytes = 0;
     void* h_b = nullptr;  size_t h_b_bytes = 0;
     void* h_c = nullptr;  size_t h_c_bytes = 0;
+    // Result flags of the device CSR -> BSR conversion.
+    void* conv_flags = nullptr; size_t conv_flags_bytes = 0;
     std::mutex mu;
 };
 

@@ -4,16 +4,19 @@
 // spmm_tiled_v4.cu): same product, same per-element arithmetic (a sequential FP32 FMA chain
 // over the row's nonzeros), new work distribution and memory access.
 //
-// The product is a gather: every nonzero (k, v) of row i reads the whole B row k (N floats)
-// and adds v * B[k, :] into C[i, :]. On B200 that gather is served by L2 (B is re-read once
-// per nonzero), so the kernels are built to keep many wide, coalesced B-row loads in flight:
-//   * a warp owns a run of columns of one C row; each lane owns VEC consecutive columns per
-//     R strides of 32*VEC, so one nonzero costs R vector loads per lane, all coalesced;
-//   * the row's (col, val) pairs are fetched 32 at a time, one pair per lane, with the next
-//     group prefetched while the current one is consumed; pairs reach the other lanes by
-//     warp shuffle;
-//   * U nonzeros' B-row loads are issued before their FMAs, in nonzero order, so the FMA
-//     chain per element stays sequential (bit-identical to the reference's order).
+// The product is a gather: every nonzero (k, v) of row i reads B row k and adds v * B[k, :]
+// into C[i, :]. B is re-read once per nonzero, so the kernels are built around the L2:
+//   * column slabs: the grid's y dimension walks N in slabs of W <= 256 columns; CTAs are
+//     issued slab by slab, so a narrower slab (tuning) keeps its B columns L2-resident at the
+//     price of re-reading A. B loads carry an L2 evict-last policy, the streamed A arrays
+//     and C stores evict-first hints;
+//   * inside a slab a warp owns one C row: each lane holds VEC consecutive columns per stride,
+//     R strides of 32*VEC columns (W = 32*VEC*R), so one nonzero costs R coalesced
+//     VEC-wide loads per lane;
+//   * the row's (col, val) pairs are fetched 32 at a time, one pair per lane, the next group
+//     prefetched while the current one is consumed, and broadcast by warp shuffle;
+//   * U nonzeros' B loads are issued before their FMAs, in nonzero order, so the FMA chain
+//     per element stays sequential (bit-identical to the reference's order).
 //
 // Two work distributions:
 //   ROWWARP  one warp per row, grid-stride over rows.
@@ -22,8 +25,8 @@
 //            belongs to the chunk holding its first item. Rows with more than S nonzeros
 //            ("long" rows) are cut at every multiple of S; each piece is summed from zero by
 //            its chunk's warp, written to a workspace slot, and the last piece to arrive
-//            (a per-row arrival counter) adds the pieces left to right and writes C. The
-//            counter is reset by that last arrival, so the workspace is all-zero between
+//            (a per-row, per-slab arrival counter) adds the pieces left to right and writes
+//            C. That last arrival resets the counter, so the workspace is all-zero between
 //            calls. No float atomics: results are deterministic.
 //
 // Every index read from A is range-checked; a bad index is recorded in the device error
@@ -35,6 +38,12 @@
 #include <cstdint>
 
 #include "common.cuh"
+
+// Resident CTAs per SM the register allocation is sized for (256 threads per CTA; 4 caps a
+// thread at 64 registers). The default chunk size assumes exactly this residency.
+#ifndef SPMM_CSR_MIN_CTAS
+#define SPMM_CSR_MIN_CTAS 4
+#endif
 
 namespace spmm_b200 {
 namespace {
@@ -54,15 +63,30 @@ struct CsrArgs {
     int S;               // merge-path chunk (items per warp) == long-row threshold
     long long items;     // M + nnz
     int num_chunks;
-    int* counters;       // num_chunks, all-zero between calls
+    int* counters;       // num_chunks per slab, all-zero between calls
     float* partials;     // num_chunks * 2 * N
+    int b_policy;        // B loads: 0 L2 evict-last, 1 plain, 2 evict-last + no L1 allocation
     DeviceErrorRecord* err;
 };
+
+__device__ __forceinline__ uint64_t evict_last_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 
 template <int VEC> struct Vec;
 template <> struct Vec<1> {
     using T = float;
-    __device__ static T load(const float* p) { return __ldg(p); }
+    __device__ static T load(const float* p, uint64_t pol, int mode) {
+        float v;
+        if (mode == 1) return __ldg(p);
+        if (mode == 2)
+            asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
+        else
+            asm volatile("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
+        return v;
+    }
     __device__ static T loadcg(const float* p) { return __ldcg(p); }
     __device__ static void store_cs(float* p, T v) { __stcs(p, v); }
     __device__ static void store_cg(float* p, T v) { __stcg(p, v); }
@@ -71,7 +95,19 @@ template <> struct Vec<1> {
 };
 template <> struct Vec<2> {
     using T = float2;
-    __device__ static T load(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
+    __device__ static T load(const float* p, uint64_t pol, int mode) {
+        float2 v;
+        if (mode == 1) return __ldg(reinterpret_cast<const float2*>(p));
+        if (mode == 2)
+            asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;"
+                         : "=f"(v.x), "=f"(v.y)
+                         : "l"(p), "l"(pol));
+        else
+            asm volatile("ld.global.nc.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;"
+                         : "=f"(v.x), "=f"(v.y)
+                         : "l"(p), "l"(pol));
+        return v;
+    }
     __device__ static T loadcg(const float* p) { return __ldcg(reinterpret_cast<const float2*>(p)); }
     __device__ static void store_cs(float* p, T v) { __stcs(reinterpret_cast<float2*>(p), v); }
     __device__ static void store_cg(float* p, T v) { __stcg(reinterpret_cast<float2*>(p), v); }
@@ -80,7 +116,19 @@ template <> struct Vec<2> {
 };
 template <> struct Vec<4> {
     using T = float4;
-    __device__ static T load(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+    __device__ static T load(const float* p, uint64_t pol, int mode) {
+        float4 v;
+        if (mode == 1) return __ldg(reinterpret_cast<const float4*>(p));
+        if (mode == 2)
+            asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                         : "l"(p), "l"(pol));
+        else
+            asm volatile("ld.global.nc.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                         : "l"(p), "l"(pol));
+        return v;
+    }
     __device__ static T loadcg(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
     __device__ static void store_cs(float* p, T v) { __stcs(reinterpret_cast<float4*>(p), v); }
     __device__ static void store_cg(float* p, T v) { __stcg(reinterpret_cast<float4*>(p), v); }
@@ -90,7 +138,7 @@ template <> struct Vec<4> {
     }
 };
 
-// Columns of lane `lane` in stride r of a pass starting at col0.
+// First column of lane `lane` in stride r of the slab starting at col0.
 template <int VEC>
 __device__ __forceinline__ int lane_col(int col0, int r, int lane) {
     return col0 + (r * 32 + lane) * VEC;
@@ -98,12 +146,13 @@ __device__ __forceinline__ int lane_col(int col0, int r, int lane) {
 
 __device__ __forceinline__ int clampi(int x, int lo, int hi) { return x < lo ? lo : (x > hi ? hi : x); }
 
-// Sum of v_p * B[col_p, cols] over p in [p0, p1) into acc (caller zeroes acc), as one
-// sequential FMA chain per column.
+// Sum of v_p * B[col_p, slab columns] over p in [p0, p1) into acc (caller zeroes acc), as
+// one sequential FMA chain per column.
 template <int VEC, int R, int U>
-__device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int col0, int lane,
+__device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int col0, int lane, uint64_t pol,
                                            float (&acc)[R][VEC]) {
     using V = Vec<VEC>;
+    const int hint = a.b_policy;
     bool ok[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) ok[r] = lane_col<VEC>(col0, r, lane) < a.N;
@@ -140,7 +189,7 @@ __device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int
                 const float* brow = Bp + static_cast<size_t>(k) * a.N;
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
-                    if (ok[r]) b[u][r] = V::load(brow + r * 32 * VEC);
+                    if (ok[r]) b[u][r] = V::load(brow + r * 32 * VEC, pol, hint);
                     else b[u][r] = typename V::T{};
                 }
             }
@@ -160,7 +209,7 @@ __device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 if (ok[r]) {
-                    const typename V::T b = V::load(brow + r * 32 * VEC);
+                    const typename V::T b = V::load(brow + r * 32 * VEC, pol, hint);
 #pragma unroll
                     for (int e = 0; e < VEC; ++e) acc[r][e] = fmaf(v, V::get(b, e), acc[r][e]);
                 }
@@ -173,7 +222,8 @@ __device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int
 }
 
 template <int VEC, int R>
-__device__ __forceinline__ void store_row(const CsrArgs& a, float* dst, int col0, int lane, const float (&acc)[R][VEC]) {
+__device__ __forceinline__ void store_slab(const CsrArgs& a, float* dst, int col0, int lane,
+                                           const float (&acc)[R][VEC], bool streaming) {
     using V = Vec<VEC>;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -182,25 +232,18 @@ __device__ __forceinline__ void store_row(const CsrArgs& a, float* dst, int col0
             typename V::T t;
 #pragma unroll
             for (int e = 0; e < VEC; ++e) V::set(t, e, acc[r][e]);
-            V::store_cs(dst + c, t);
+            if (streaming) V::store_cs(dst + c, t);
+            else V::store_cg(dst + c, t);
         }
     }
 }
 
-// Full row i: C[i, :] = A[i, :] * B.
-template <int VEC, int R, int U>
-__device__ __forceinline__ void full_row(const CsrArgs& a, int i, int rs, int re, int lane) {
-    constexpr int W = 32 * VEC * R;
-    float* crow = a.C + static_cast<size_t>(i) * a.N;
-    for (int col0 = 0; col0 < a.N; col0 += W) {
-        float acc[R][VEC];
+template <int VEC, int R>
+__device__ __forceinline__ void zero(float (&acc)[R][VEC]) {
 #pragma unroll
-        for (int r = 0; r < R; ++r)
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) acc[r][e] = 0.f;
-        accumulate<VEC, R, U>(a, rs, re, col0, lane, acc);
-        store_row<VEC, R>(a, crow, col0, lane, acc);
-    }
+        for (int e = 0; e < VEC; ++e) acc[r][e] = 0.f;
 }
 
 // Row bounds clamped into [0, nnz] with re >= rs (malformed row_ptr is recorded).
@@ -214,14 +257,20 @@ __device__ __forceinline__ void row_bounds(const CsrArgs& a, int i, int& rs, int
 }
 
 template <int VEC, int R, int U>
-__global__ void __launch_bounds__(kThreads) csr_rowwarp_kernel(CsrArgs a) {
+__global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kernel(CsrArgs a) {
+    constexpr int W = 32 * VEC * R;
     const int lane = threadIdx.x & 31;
     const int warp = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
     const int nwarps = gridDim.x * kWarpsPerCta;
+    const int col0 = blockIdx.y * W;
+    const uint64_t pol = evict_last_policy();
     for (int i = warp; i < a.M; i += nwarps) {
         int rs, re;
         row_bounds(a, i, rs, re);
-        full_row<VEC, R, U>(a, i, rs, re, lane);
+        float acc[R][VEC];
+        zero(acc);
+        accumulate<VEC, R, U>(a, rs, re, col0, lane, pol, acc);
+        store_slab<VEC, R>(a, a.C + static_cast<size_t>(i) * a.N, col0, lane, acc, true);
     }
 }
 
@@ -247,31 +296,31 @@ __device__ __forceinline__ int warp_lower_bound(const CsrArgs& a, long long d, i
     return lo;
 }
 
-// One piece [p0, p1) of long row i (rs..re); `slot` is this chunk's workspace slot.
-template <int VEC, int R, int U>
-__device__ __forceinline__ void long_piece(const CsrArgs& a, int i, int rs, int re, int p0, int p1, int slot, int lane) {
-    using V = Vec<VEC>;
-    constexpr int W = 32 * VEC * R;
-    float* mine = a.partials + static_cast<size_t>(slot) * a.N;
-    for (int col0 = 0; col0 < a.N; col0 += W) {
-        float acc[R][VEC];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) acc[r][e] = 0.f;
-        accumulate<VEC, R, U>(a, p0, p1, col0, lane, acc);
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const int c = lane_col<VEC>(col0, r, lane);
-            if (c < a.N) {
-                typename V::T t;
-#pragma unroll
-                for (int e = 0; e < VEC; ++e) V::set(t, e, acc[r][e]);
-                V::store_cg(mine + c, t);
-            }
-        }
+// First row r >= r0 with r + row_ptr[r] >= d (M if none): a chunk spans few rows, so scan
+// forward 32 rows per coalesced probe; after 4 probes fall back to the search.
+__device__ __forceinline__ int warp_forward_bound(const CsrArgs& a, int r0, long long d, int lane) {
+    int r = r0;
+    for (int step = 0; step < 4 && r < a.M; ++step, r += 32) {
+        const int cand = r + lane;
+        const bool lt = cand < a.M && static_cast<long long>(cand) + __ldg(a.row_ptr + cand) < d;
+        const unsigned m = __ballot_sync(kFull, lt);
+        if (m != kFull) return r + __popc(m);
     }
-    // Publish the piece, then count arrivals on the row's first chunk.
+    if (r >= a.M) return a.M;
+    return warp_lower_bound(a, d, lane);
+}
+
+// One piece [p0, p1) of long row i (rs..re) for this CTA's slab; `slot` is this chunk's
+// workspace slot.
+template <int VEC, int R, int U>
+__device__ __forceinline__ void long_piece(const CsrArgs& a, int i, int rs, int re, int p0, int p1, int slot,
+                                           int col0, int lane, uint64_t pol) {
+    using V = Vec<VEC>;
+    float acc[R][VEC];
+    zero(acc);
+    accumulate<VEC, R, U>(a, p0, p1, col0, lane, pol, acc);
+    store_slab<VEC, R>(a, a.partials + static_cast<size_t>(slot) * a.N, col0, lane, acc, false);
+    // Publish the piece, then count arrivals on the row's first chunk (per slab).
     __threadfence();
     __syncwarp();
     const long long first_item = static_cast<long long>(i) + rs;
@@ -279,40 +328,48 @@ __device__ __forceinline__ void long_piece(const CsrArgs& a, int i, int rs, int 
     const int ca = static_cast<int>(first_item / a.S);
     const int cb = static_cast<int>(last_item / a.S);
     const int pieces = cb - ca + 1;
+    int* counter = a.counters + static_cast<size_t>(blockIdx.y) * a.num_chunks + ca;
     int prev = 0;
-    if (lane == 0) prev = atomicAdd(a.counters + ca, 1);
+    if (lane == 0) prev = atomicAdd(counter, 1);
     prev = __shfl_sync(kFull, prev, 0);
     if (prev != pieces - 1) return;
-    // Last arrival: add the pieces in chunk order and write the row.
+    // Last arrival: add the pieces in chunk order and write the row's slab; clear every slot
+    // it read and the counter, so the whole workspace is zero again after the launch.
     __threadfence();
     float* crow = a.C + static_cast<size_t>(i) * a.N;
-    for (int col0 = 0; col0 < a.N; col0 += W) {
+    const typename V::T zero_v{};
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const int c = lane_col<VEC>(col0, r, lane);
-            if (c < a.N) {
-                typename V::T s = V::loadcg(a.partials + static_cast<size_t>(2 * ca + 1) * a.N + c);
-                for (int cc = ca + 1; cc <= cb; ++cc) {
-                    const typename V::T t = V::loadcg(a.partials + static_cast<size_t>(2 * cc) * a.N + c);
+    for (int r = 0; r < R; ++r) {
+        const int c = lane_col<VEC>(col0, r, lane);
+        if (c < a.N) {
+            float* first = a.partials + static_cast<size_t>(2 * ca + 1) * a.N + c;
+            typename V::T s = V::loadcg(first);
+            V::store_cg(first, zero_v);
+            for (int cc = ca + 1; cc <= cb; ++cc) {
+                float* slot_p = a.partials + static_cast<size_t>(2 * cc) * a.N + c;
+                const typename V::T t = V::loadcg(slot_p);
+                V::store_cg(slot_p, zero_v);
 #pragma unroll
-                    for (int e = 0; e < VEC; ++e) V::set(s, e, V::get(s, e) + V::get(t, e));
-                }
-                V::store_cs(crow + c, s);
+                for (int e = 0; e < VEC; ++e) V::set(s, e, V::get(s, e) + V::get(t, e));
             }
+            V::store_cs(crow + c, s);
         }
     }
-    if (lane == 0) a.counters[ca] = 0;
+    if (lane == 0) *counter = 0;
 }
 
 template <int VEC, int R, int U>
-__global__ void __launch_bounds__(kThreads) csr_merge_kernel(CsrArgs a) {
+__global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(CsrArgs a) {
+    constexpr int W = 32 * VEC * R;
     const int lane = threadIdx.x & 31;
     const int c = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
     if (c >= a.num_chunks) return;
+    const int col0 = blockIdx.y * W;
+    const uint64_t pol = evict_last_policy();
     const long long d0 = static_cast<long long>(c) * a.S;
     const long long d1 = min(d0 + a.S, a.items);
     const int r0 = warp_lower_bound(a, d0, lane);
-    const int r1 = warp_lower_bound(a, d1, lane);
+    const int r1 = warp_forward_bound(a, r0, d1, lane);
 
     // A long row that started in an earlier chunk and reaches into this one.
     if (r0 > 0) {
@@ -322,7 +379,7 @@ __global__ void __launch_bounds__(kThreads) csr_merge_kernel(CsrArgs a) {
         if (qe - qs > a.S) {
             const int p0 = static_cast<int>(max(static_cast<long long>(qs), d0 - q));
             const int p1 = static_cast<int>(min(static_cast<long long>(qe), d1 - q));
-            if (p0 < p1) long_piece<VEC, R, U>(a, q, qs, qe, p0, p1, 2 * c, lane);
+            if (p0 < p1) long_piece<VEC, R, U>(a, q, qs, qe, p0, p1, 2 * c, col0, lane, pol);
         }
     }
     // Rows whose first item lies in this chunk.
@@ -330,10 +387,13 @@ __global__ void __launch_bounds__(kThreads) csr_merge_kernel(CsrArgs a) {
         int rs, re;
         row_bounds(a, i, rs, re);
         if (re - rs <= a.S) {
-            full_row<VEC, R, U>(a, i, rs, re, lane);
+            float acc[R][VEC];
+            zero(acc);
+            accumulate<VEC, R, U>(a, rs, re, col0, lane, pol, acc);
+            store_slab<VEC, R>(a, a.C + static_cast<size_t>(i) * a.N, col0, lane, acc, true);
         } else {
             const int p1 = static_cast<int>(min(static_cast<long long>(re), d1 - i));
-            long_piece<VEC, R, U>(a, i, rs, re, rs, max(p1, rs), 2 * c + 1, lane);
+            long_piece<VEC, R, U>(a, i, rs, re, rs, max(p1, rs), 2 * c + 1, col0, lane, pol);
         }
     }
 }
@@ -345,34 +405,53 @@ __global__ void __launch_bounds__(kThreads) csr_merge_kernel(CsrArgs a) {
 struct Geometry {
     int vec = 1;
     int r = 1;
+    int width() const { return 32 * vec * r; }
 };
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-Geometry pick_geometry(const float* B, const float* C, int N, int col_pass) {
+// Slab width: the narrowest of 32/64/128/256 columns that covers N, at most 256. Narrower
+// slabs that keep a slab's B columns L2-resident (col_pass) re-read A once per slab; on B200
+// at config 5 (B = 134 MB) one 256-wide slab with evict-last B loads measured faster than two
+// 128-wide ones (1.02 vs 1.13 ms), so N is not split further by default.
+int slab_width(int N, int col_pass) {
+    if (col_pass > 0) return col_pass;
+    int w = 32;
+    while (w < N && w < 256) w *= 2;
+    return w;
+}
+
+// Realise a slab width with the widest vector the operands allow.
+Geometry pick_geometry(const float* B, const float* C, int N, int w) {
     Geometry g;
-    const bool a16 = aligned(B, 16) && aligned(C, 16);
-    const bool a8 = aligned(B, 8) && aligned(C, 8);
-    if (N % 4 == 0 && a16 && (N >= 128 || col_pass >= 128)) g.vec = 4;
-    else if (N % 2 == 0 && a8 && (N >= 64 || col_pass >= 64)) g.vec = 2;
-    else g.vec = 1;
-    const int want = col_pass > 0 ? col_pass : N;
-    const int per = 32 * g.vec;
-    int r = (want + per - 1) / per;
-    const int rmax = g.vec == 1 ? 4 : 2;
-    if (r > rmax) r = rmax;
-    if (r == 3) r = 4;
-    if (g.vec != 1 && r > 2) r = 2;
-    if (r < 1) r = 1;
-    g.r = r;
+    const bool v4 = N % 4 == 0 && aligned(B, 16) && aligned(C, 16);
+    const bool v2 = N % 2 == 0 && aligned(B, 8) && aligned(C, 8);
+    if (w >= 256) {
+        if (v4) { g.vec = 4; g.r = 2; }
+        else if (v2) { g.vec = 2; g.r = 4; }
+        else { g.vec = 1; g.r = 8; }
+    } else if (w >= 128) {
+        if (v4) { g.vec = 4; g.r = 1; }
+        else if (v2) { g.vec = 2; g.r = 2; }
+        else { g.vec = 1; g.r = 4; }
+    } else if (w >= 64) {
+        if (v2) { g.vec = 2; g.r = 1; }
+        else { g.vec = 1; g.r = 2; }
+    } else {
+        g.vec = 1;
+        g.r = 1;
+    }
     return g;
 }
 
+// One chunk per resident warp: the grid is a single wave (SMs x SPMM_CSR_MIN_CTAS CTAs of 8
+// warps), every warp gets the same number of merge-path items, no tail wave. Multiple of 32,
+// at least 64.
 int default_chunk(long long items, int sm_count) {
-    // Aim at ~32 chunks per SM in one wave, in multiples of 32 items, within [64, 2048].
-    const long long target = items / (static_cast<long long>(std::max(sm_count, 1)) * 32);
-    long long s = ((target + 31) / 32) * 32;
-    s = std::max<long long>(64, std::min<long long>(2048, s));
+    const long long warps = static_cast<long long>(std::max(sm_count, 1)) * SPMM_CSR_MIN_CTAS * kWarpsPerCta;
+    long long s = (items + warps - 1) / warps;
+    s = ((s + 31) / 32) * 32;
+    s = std::max<long long>(64, std::min<long long>(1ll << 30, s));
     return static_cast<int>(s);
 }
 
@@ -398,31 +477,40 @@ int check_tune(const spmm_csr_tuning* tune) {
     if (tune->col_pass != 0 && tune->col_pass != 32 && tune->col_pass != 64 && tune->col_pass != 128 &&
         tune->col_pass != 256)
         return SPMM_ERR_INVALID_ARG;
+    if (tune->b_policy < 0 || tune->b_policy > 2) return SPMM_ERR_INVALID_ARG;
     return SPMM_OK;
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Counters for every slab the narrowest slab width (32 columns) could need, so the size does
+// not depend on the operands' alignment.
+size_t counter_bytes(long long num_chunks, int N) {
+    return align_up(static_cast<size_t>(num_chunks) * static_cast<size_t>((N + 31) / 32) * sizeof(int), 256);
+}
+
 size_t merge_workspace_bytes(long long num_chunks, int N) {
     if (num_chunks <= 0) return 0;
-    return align_up(static_cast<size_t>(num_chunks) * sizeof(int), 256) +
-           static_cast<size_t>(num_chunks) * 2 * static_cast<size_t>(N) * sizeof(float);
+    return counter_bytes(num_chunks, N) + static_cast<size_t>(num_chunks) * 2 * static_cast<size_t>(N) * sizeof(float);
 }
 
 template <int VEC, int R>
-void launch_vr(int algo, const CsrArgs& a, int grid, cudaStream_t s) {
-    constexpr int U = (R == 1) ? 8 : (R == 2 ? 4 : 2);
+void launch_vr(int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
+    // Eight vector loads per lane in flight: U nonzeros x R strides.
+    constexpr int U = (8 / R) > 0 ? (8 / R) : 1;
     if (algo == SPMM_CSR_ROWWARP) csr_rowwarp_kernel<VEC, R, U><<<grid, kThreads, 0, s>>>(a);
     else csr_merge_kernel<VEC, R, U><<<grid, kThreads, 0, s>>>(a);
 }
 
-void launch(const Geometry& g, int algo, const CsrArgs& a, int grid, cudaStream_t s) {
+void launch(const Geometry& g, int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
     switch (g.vec * 10 + g.r) {
         case 11: launch_vr<1, 1>(algo, a, grid, s); break;
         case 12: launch_vr<1, 2>(algo, a, grid, s); break;
         case 14: launch_vr<1, 4>(algo, a, grid, s); break;
+        case 18: launch_vr<1, 8>(algo, a, grid, s); break;
         case 21: launch_vr<2, 1>(algo, a, grid, s); break;
         case 22: launch_vr<2, 2>(algo, a, grid, s); break;
+        case 24: launch_vr<2, 4>(algo, a, grid, s); break;
         case 41: launch_vr<4, 1>(algo, a, grid, s); break;
         default: launch_vr<4, 2>(algo, a, grid, s); break;
     }
@@ -430,7 +518,7 @@ void launch(const Geometry& g, int algo, const CsrArgs& a, int grid, cudaStream_
 
 }  // namespace
 
-// Shared by the C entry points below and by the no-workspace variants in other files.
+// Shared by the C entry points below and by the allocation-free variant in noalloc.cu.
 int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
                    const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream,
                    DeviceState* st) {
@@ -451,12 +539,16 @@ int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, 
     a.B = B;
     a.C = C;
     a.err = st->err;
-    const Geometry g = pick_geometry(B, C, N, tune ? tune->col_pass : 0);
+    a.b_policy = tune ? tune->b_policy : 0;
+    const int w = slab_width(N, tune ? tune->col_pass : 0);
+    const Geometry g = pick_geometry(B, C, N, w);
+    const int slabs = (N + g.width() - 1) / g.width();
+    if (slabs > 65535) return SPMM_ERR_TOO_LARGE;
 
-    int grid = 0;
+    dim3 grid(1, slabs, 1);
     if (algo == SPMM_CSR_ROWWARP) {
         const long long warps = std::min<long long>(A->rows, static_cast<long long>(st->sm_count) * 64);
-        grid = static_cast<int>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
+        grid.x = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
     } else {
         a.S = resolve_chunk(A, tune, st->sm_count);
         a.items = static_cast<long long>(A->rows) + A->nnz;
@@ -466,8 +558,8 @@ int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, 
         const size_t need = merge_workspace_bytes(chunks, N);
         if (need > ws_bytes || (need > 0 && !ws)) return SPMM_ERR_INVALID_ARG;
         a.counters = static_cast<int*>(ws);
-        a.partials = reinterpret_cast<float*>(static_cast<char*>(ws) + align_up(static_cast<size_t>(chunks) * sizeof(int), 256));
-        grid = static_cast<int>((chunks + kWarpsPerCta - 1) / kWarpsPerCta);
+        a.partials = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_bytes(chunks, N));
+        grid.x = static_cast<unsigned>((chunks + kWarpsPerCta - 1) / kWarpsPerCta);
     }
     launch(g, algo, a, grid, stream);
     SPMM_CUDA_TRY(cudaGetLastError());
@@ -486,6 +578,13 @@ int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, con
     const long long items = static_cast<long long>(A->rows) + A->nnz;
     *bytes = merge_workspace_bytes((items + S - 1) / S, N);
     return SPMM_OK;
+}
+
+// Bytes at the start of the merge-path workspace that must be zero when a launch starts.
+size_t csr_f32_counter_bytes(const spmm_csr_view* A, int32_t N, const spmm_csr_tuning* tune, int sm_count) {
+    const int S = resolve_chunk(A, tune, sm_count);
+    const long long items = static_cast<long long>(A->rows) + A->nnz;
+    return counter_bytes((items + S - 1) / S, N);
 }
 
 int csr_f32_chunk(const spmm_csr_view* A, const spmm_csr_tuning* tune, int sm_count) {

@@ -28,7 +28,7 @@ int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, 
                    const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream, DeviceState* st);
 int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, const spmm_csr_tuning* tune,
                             int sm_count, size_t* bytes);
-int csr_f32_chunk(const spmm_csr_view* A, const spmm_csr_tuning* tune, int sm_count);
+size_t csr_f32_counter_bytes(const spmm_csr_view* A, int32_t N, const spmm_csr_tuning* tune, int sm_count);
 
 namespace {
 
@@ -82,12 +82,10 @@ extern "C" int spmm_csr_f32_noalloc(const spmm_csr_view* A, const float* B, floa
     void* scratch = nullptr;
     SPMM_TRY(scratch_address(device, &scratch));
     if (need > 0) {
-        // The merge-path workspace starts with one arrival counter per chunk (padded to 256
-        // bytes); only those must be zero when the kernel starts.
-        const long long items = static_cast<long long>(A->rows) + A->nnz;
-        const long long chunk = csr_f32_chunk(A, nullptr, local.sm_count);
-        const size_t counter_bytes = (static_cast<size_t>((items + chunk - 1) / chunk) * sizeof(int) + 255) / 256 * 256;
-        SPMM_CUDA_TRY(cudaMemsetAsync(scratch, 0, counter_bytes < need ? counter_bytes : need, as_stream(stream)));
+        // The merge-path workspace starts with the arrival counters (one per chunk and
+        // column slab); only those must be zero when the kernel starts.
+        const size_t counters = csr_f32_counter_bytes(A, N, nullptr, local.sm_count);
+        SPMM_CUDA_TRY(cudaMemsetAsync(scratch, 0, counters < need ? counters : need, as_stream(stream)));
     }
     return csr_f32_launch(A, B, C, N, algo, nullptr, scratch, need, as_stream(stream), &local);
 }

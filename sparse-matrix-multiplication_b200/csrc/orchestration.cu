@@ -225,30 +225,48 @@ int spmm_hybrid_run(const spmm_hybrid_plan* plan, const spmm_csr_view* hA, const
             break;
         }
         if (plan->backend == SPMM_BACKEND_TC) {
-            spmm_bsr_host hb{};
-            if (fail(spmm_csr_to_bsr16_host(hA, SPMM_DTYPE_F16, &hb)) != SPMM_OK) break;
+            // The BSR is built once, on the GPU, from the uploaded CSR (the host conversion is
+            // the fallback for rows with unsorted columns or K > 1,048,576).
+            const int br = (hA->rows + 15) / 16;
             int* brp = nullptr;
             int* bci = nullptr;
             uint16_t* bv = nullptr;
             uint16_t* b16 = nullptr;
-            const size_t nb = hb.num_blocks;
-            if (cudaMalloc(&brp, sizeof(int) * (hb.block_rows + 1)) != cudaSuccess ||
-                cudaMalloc(&bci, sizeof(int) * std::max<size_t>(nb, 1)) != cudaSuccess ||
-                cudaMalloc(&bv, sizeof(uint16_t) * std::max<size_t>(nb * 256, 1)) != cudaSuccess ||
+            int nb = 0;
+            DeviceCsr d;
+            spmm_bsr_host hb{};
+            if (cudaMalloc(&brp, sizeof(int) * (br + 1)) != cudaSuccess ||
                 cudaMalloc(&b16, sizeof(uint16_t) * std::max<size_t>(K * N, 1)) != cudaSuccess) {
                 rc = SPMM_ERR_NO_MEMORY;
-            } else {
-                cudaMemcpyAsync(brp, hb.row_ptr, sizeof(int) * (hb.block_rows + 1), cudaMemcpyHostToDevice, s);
-                if (nb) {
-                    cudaMemcpyAsync(bci, hb.col_idx, sizeof(int) * nb, cudaMemcpyHostToDevice, s);
-                    cudaMemcpyAsync(bv, hb.values, sizeof(uint16_t) * nb * 256, cudaMemcpyHostToDevice, s);
-                }
-                rc = spmm_convert_f32(dB, b16, static_cast<int64_t>(K) * N, SPMM_DTYPE_F16, s);
+            } else if ((rc = upload_csr(hA, &d, s)) == SPMM_OK) {
+                rc = spmm_csr_to_bsr16_device_count(&d.view, brp, &nb, s);
                 if (rc == SPMM_OK) {
-                    spmm_bsr_view v{hb.rows, hb.cols, hb.block_rows, hb.block_cols, hb.num_blocks, hb.nnz, brp, bci, bv,
-                                    SPMM_DTYPE_F16};
-                    rc = time_launches([&] { return bsr16_launch(&v, b16, dC, N, 0, s, st); }, warmup, iters, s, ms);
+                    if (cudaMalloc(&bci, sizeof(int) * std::max(nb, 1)) != cudaSuccess ||
+                        cudaMalloc(&bv, sizeof(uint16_t) * std::max<size_t>(static_cast<size_t>(nb) * 256, 2)) !=
+                            cudaSuccess)
+                        rc = SPMM_ERR_NO_MEMORY;
+                    else
+                        rc = spmm_csr_to_bsr16_device_fill(&d.view, brp, bci, bv, SPMM_DTYPE_F16, s);
+                } else if (rc == SPMM_ERR_UNSUPPORTED && (rc = spmm_csr_to_bsr16_host(hA, SPMM_DTYPE_F16, &hb)) == SPMM_OK) {
+                    nb = hb.num_blocks;
+                    if (cudaMalloc(&bci, sizeof(int) * std::max(nb, 1)) != cudaSuccess ||
+                        cudaMalloc(&bv, sizeof(uint16_t) * std::max<size_t>(static_cast<size_t>(nb) * 256, 2)) !=
+                            cudaSuccess) {
+                        rc = SPMM_ERR_NO_MEMORY;
+                    } else {
+                        cudaMemcpyAsync(brp, hb.row_ptr, sizeof(int) * (br + 1), cudaMemcpyHostToDevice, s);
+                        if (nb) {
+                            cudaMemcpyAsync(bci, hb.col_idx, sizeof(int) * nb, cudaMemcpyHostToDevice, s);
+                            cudaMemcpyAsync(bv, hb.values, sizeof(uint16_t) * nb * 256, cudaMemcpyHostToDevice, s);
+                        }
+                    }
                 }
+            }
+            if (rc == SPMM_OK) rc = spmm_convert_f32(dB, b16, static_cast<int64_t>(K) * N, SPMM_DTYPE_F16, s);
+            if (rc == SPMM_OK) {
+                spmm_bsr_view v{hA->rows, hA->cols, br, static_cast<int32_t>((K + 15) / 16), nb, hA->nnz, brp, bci, bv,
+                                SPMM_DTYPE_F16};
+                rc = time_launches([&] { return bsr16_launch(&v, b16, dC, N, 0, s, st); }, warmup, iters, s, ms);
             }
             cudaStreamSynchronize(s);
             cudaFree(brp);

@@ -36,7 +36,7 @@ EXPORTS = [
     "spmm_csr_f32_ws", "spmm_csr_f32_chunk", "spmm_csr_f32_host", "spmm_convert_f32", "spmm_bsr16",
     "spmm_bsr16_algo", "spmm_device_error", "spmm_hybrid_default_threshold", "spmm_hybrid_choose",
     "spmm_backend_name", "spmm_hybrid_run", "spmm_gpu_count", "spmm_multigpu_run", "spmm_unified_run",
-    "spmm_csr_f32_noalloc",
+    "spmm_csr_f32_noalloc", "spmm_csr_to_bsr16_device_count", "spmm_csr_to_bsr16_device_fill",
 ]
 
 
@@ -75,7 +75,7 @@ class BsrStats(C.Structure):
 
 
 class CsrTuning(C.Structure):
-    _fields_ = [("chunk", C.c_int32), ("col_pass", C.c_int32), ("reserved", C.c_int32 * 6)]
+    _fields_ = [("chunk", C.c_int32), ("col_pass", C.c_int32), ("b_policy", C.c_int32), ("reserved", C.c_int32 * 5)]
 
 
 class HybridPlan(C.Structure):
@@ -132,6 +132,8 @@ def lib() -> C.CDLL:
                                         C.POINTER(i32), vp, vp, C.POINTER(f32)]),
         "spmm_unified_run": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, i32, C.POINTER(f32)]),
         "spmm_csr_f32_noalloc": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, vp]),
+        "spmm_csr_to_bsr16_device_count": (C.c_int, [C.POINTER(CsrView), vp, C.POINTER(i32), vp]),
+        "spmm_csr_to_bsr16_device_fill": (C.c_int, [C.POINTER(CsrView), vp, vp, vp, i32, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -358,6 +360,25 @@ def convert_f32(src, dst, n: int, dtype: int = DTYPE_F16, stream=None) -> None:
 
 def bsr16(A: BsrView, B16, Cout, N: int, algo: int = 0, stream=None) -> None:
     check(lib().spmm_bsr16_algo(C.byref(A), ptr(B16), ptr(Cout), N, algo, stream_ptr(stream)), "spmm_bsr16")
+
+
+def csr_to_bsr16_device(A: CsrView, dtype: int = DTYPE_F16, stream=None):
+    """CSR (device view) -> BSR-16 on the GPU. Returns (BsrView, [row_ptr, col_idx, values]
+    torch tensors that own the memory)."""
+    import torch
+
+    br = (A.rows + 15) // 16
+    rp = torch.empty(br + 1, dtype=torch.int32, device="cuda")
+    nb = C.c_int32()
+    check(lib().spmm_csr_to_bsr16_device_count(C.byref(A), ptr(rp), C.byref(nb), stream_ptr(stream)),
+          "spmm_csr_to_bsr16_device_count")
+    n = int(nb.value)
+    ci = torch.empty(max(n, 1), dtype=torch.int32, device="cuda")
+    vals = torch.empty(max(n * 256, 2), dtype=torch.int16, device="cuda")
+    check(lib().spmm_csr_to_bsr16_device_fill(C.byref(A), ptr(rp), ptr(ci), ptr(vals), dtype, stream_ptr(stream)),
+          "spmm_csr_to_bsr16_device_fill")
+    view = BsrView(A.rows, A.cols, br, (A.cols + 15) // 16, n, A.nnz, ptr(rp), ptr(ci), ptr(vals), dtype)
+    return view, [rp, ci, vals]
 
 
 def device_error(device: int = 0, clear: bool = True) -> tuple[int, int]:

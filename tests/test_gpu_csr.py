@@ -48,10 +48,11 @@ def run(torch, A: S.HostCSR, B: np.ndarray, algo=S.CSR_AUTO, tuning=None, b_off=
 
 
 def _counters_zero(ws, view, N, tuning) -> bool:
-    """The counter block (first num_chunks ints) is zero; partial slots may hold data."""
+    """The counter block (num_chunks ints per possible 32-column slab) is zero; partial slots
+    may hold data."""
     chunk = S.csr_chunk(view, N, S.CSR_MERGE, tuning)
     chunks = (view.rows + view.nnz + chunk - 1) // chunk
-    return int(ws[: 4 * chunks].count_nonzero()) == 0
+    return int(ws[: 4 * chunks * ((N + 31) // 32)].count_nonzero()) == 0
 
 
 def chunk_of(A: S.HostCSR, N: int, tuning=None) -> int:
