@@ -266,12 +266,16 @@ def main():
         alg_bytes = 512 * Ah.num_blocks + 4 * Ah.num_blocks + 4 * (Ah.block_rows + 1) + 2 * A.cols * N + 4 * A.rows * N
         kernel_name = "bsr_tcgen05_kernel"
     else:
+        # Inspect the rank's rows once (picks the work distribution, owns the workspace).
+        plan = S.CsrPlan(view, N, stream=stream)
+        csr_algo = plan.algo
+
         def step():
-            S.csr_f32(view, Bd, Cd, N, S.CSR_AUTO, stream)
+            plan.execute(Bd, Cd, stream)
 
         # Compulsory bytes of one launch (this rank): A rows + row_ptr + all of B + C rows.
         alg_bytes = 8 * Ar.nnz + 4 * (rows_r + 1) + 4 * A.cols * N + 4 * rows_r * N
-        kernel_name = "csr_merge_kernel"
+        kernel_name = "csr_rowwarp_kernel" if csr_algo == S.CSR_ROWWARP else "csr_merge_kernel"
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev) if small else None
 
@@ -321,13 +325,13 @@ def main():
         hB = pin(Bh).numpy()
         hC = torch.empty((max(rows_r, 1), N), dtype=torch.float32).pin_memory().numpy()
         for _ in range(2):
-            S.csr_f32_host(hA, hB, hC, N, S.CSR_AUTO, stream)
+            S.csr_f32_host(hA, hB, hC, N, csr_algo, stream)
         ke = max(3, min(K, 20))
         barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for _ in range(ke):
-            S.csr_f32_host(hA, hB, hC, N, S.CSR_AUTO, stream)
+            S.csr_f32_host(hA, hB, hC, N, csr_algo, stream)
         torch.cuda.synchronize()
         e2e_ms = (time.perf_counter() - t0) * 1e3 / ke
         barrier()
@@ -340,15 +344,15 @@ def main():
 
     # ---- roofline of the dominant kernel (per launch, this rank; rank 0 reports)
     achieved = alg_bytes / (avg_launch_ms * 1e-3) / 1e9
+    # DRAM bytes per launch from the committed ncu summary of this kernel and config, for this
+    # GPU count (a line "dram_bytes_per_launch_gpus<N>: <bytes>"); null when not captured.
     traffic = None
-    prof = REPO / "profiles" / f"traffic_{cfg_name}.json"
+    prof = REPO / "profiles" / f"{kernel_name}_config{cfg_name[1:]}.md"
     if prof.exists():
-        try:
-            d = json.loads(prof.read_text())
-            per_nnz = d.get("dram_bytes_per_launch_per_gpu", {}).get(str(world))
-            traffic = per_nnz if per_nnz is not None else d.get("dram_bytes_per_launch")
-        except ValueError:
-            traffic = None
+        key = f"dram_bytes_per_launch_gpus{world}:"
+        for line in prof.read_text().splitlines():
+            if line.startswith(key):
+                traffic = int(line.split(":", 1)[1].strip())
     roofline = {"bound": "hbm", "kernel": kernel_name, "achieved": round(achieved, 1), "peak": hbm_peak,
                 "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
@@ -375,6 +379,7 @@ def main():
             "data": "synthetic (reference generators, fixed seeds)",
             "config": {"workload": CONFIGS[cfg_name], "config_id": cfg_name, "nnz": total_nnz, "N": N,
                        "rows": A.rows, "cols": A.cols, "parallelism": f"row-split x{world} (nnz-balanced)",
+                       "kernel": kernel_name,
                        "l2": "inputs larger than L2" if not small else "L2 flushed between steps",
                        "b_broadcast_ms": round(bcast_ms, 4)},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": K,

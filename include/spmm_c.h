@@ -163,7 +163,8 @@ int spmm_nnz_balanced_bounds(const int32_t* row_ptr, int32_t rows, int64_t nnz, 
 /* Tuning knobs; zero fields take the library default. chunk = merge-path items per warp
  * (a multiple of 32, 64..8192); it also sets the long-row threshold. col_pass = width of a
  * column slab (the grid walks N slab by slab so a slab's B columns stay in L2): 0 = auto,
- * else 32/64/128/256. b_policy: 0 = B loads carry an L2 evict-last hint, 1 = plain loads,
+ * else 32/64/128/256. b_policy: 0 = plain non-coherent B loads (default; measured fastest
+ * on B200 in an interleaved A/B over configs 1, 2, 4, 5), 1 = with an L2 evict-last hint,
  * 2 = evict-last and no L1 allocation. */
 typedef struct spmm_csr_tuning {
     int32_t chunk;
@@ -213,6 +214,20 @@ int spmm_csr_f32_chunk(const spmm_csr_view* A, int32_t N, int32_t algo,
 int spmm_csr_f32_noalloc(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
                          void* stream);
 
+/* Inspector / executor form of spmm_csr_f32 (no counterpart in the reference, whose
+ * launchers re-derive everything per call). spmm_csr_plan_create reads A's device row_ptr
+ * once (one small kernel, synchronises `stream`) and picks the work distribution:
+ * SPMM_CSR_ROWWARP when the longest row is at most max(4 * (M + nnz) / resident warps, 256),
+ * else SPMM_CSR_MERGE; it allocates the plan's workspace. spmm_csr_plan_execute launches only
+ * (no allocation, asynchronous); A's arrays must stay valid and unchanged. Results equal
+ * spmm_csr_f32 with the chosen algo bit for bit. */
+typedef struct spmm_csr_plan spmm_csr_plan;
+int spmm_csr_plan_create(const spmm_csr_view* A, int32_t N, const spmm_csr_tuning* tune, void* stream,
+                         spmm_csr_plan** plan);
+int spmm_csr_plan_execute(const spmm_csr_plan* plan, const float* B, float* C, void* stream);
+int spmm_csr_plan_info(const spmm_csr_plan* plan, int32_t* algo, int32_t* max_row, size_t* ws_bytes);
+void spmm_csr_plan_destroy(spmm_csr_plan* plan);
+
 /* End-to-end call on HOST buffers: copies A and B to the current device (pinned or
  * pageable host memory), computes, copies C back, synchronises `stream`. Device buffers
  * are cached by the library between calls. */
@@ -252,7 +267,8 @@ typedef struct spmm_hybrid_plan {
     const char* reason; /* static string */
 } spmm_hybrid_plan;
 
-/* Default fill-in threshold of this build (the reference's default is 2.0). */
+/* Default fill-in threshold: 6.0, the CSR / tensor-core crossover measured on B200 by
+ * sparse-matrix-multiplication_b200/sweep.py (the reference's T4 default is 2.0). */
 float spmm_hybrid_default_threshold(void);
 
 /* TC iff N % 16 == 0 && N > 0 && fill_in <= threshold. threshold <= 0 selects the default.

@@ -8,8 +8,8 @@
 // into C[i, :]. B is re-read once per nonzero, so the kernels are built around the L2:
 //   * column slabs: the grid's y dimension walks N in slabs of W <= 256 columns; CTAs are
 //     issued slab by slab, so a narrower slab (tuning) keeps its B columns L2-resident at the
-//     price of re-reading A. B loads carry an L2 evict-last policy, the streamed A arrays
-//     and C stores evict-first hints;
+//     price of re-reading A. The streamed A arrays and C stores carry evict-first hints; B
+//     loads are plain non-coherent loads by default (L2 evict-last variants are tunable);
 //   * inside a slab a warp owns one C row: each lane holds VEC consecutive columns per stride,
 //     R strides of 32*VEC columns (W = 32*VEC*R), so one nonzero costs R coalesced
 //     VEC-wide loads per lane;
@@ -65,7 +65,7 @@ struct CsrArgs {
     int num_chunks;
     int* counters;       // num_chunks per slab, all-zero between calls
     float* partials;     // num_chunks * 2 * N
-    int b_policy;        // B loads: 0 L2 evict-last, 1 plain, 2 evict-last + no L1 allocation
+    int b_policy;        // B loads: 0 plain, 1 L2 evict-last, 2 evict-last + no L1 allocation
     DeviceErrorRecord* err;
 };
 
@@ -80,7 +80,7 @@ template <> struct Vec<1> {
     using T = float;
     __device__ static T load(const float* p, uint64_t pol, int mode) {
         float v;
-        if (mode == 1) return __ldg(p);
+        if (mode == 0) return __ldg(p);
         if (mode == 2)
             asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
         else
@@ -97,7 +97,7 @@ template <> struct Vec<2> {
     using T = float2;
     __device__ static T load(const float* p, uint64_t pol, int mode) {
         float2 v;
-        if (mode == 1) return __ldg(reinterpret_cast<const float2*>(p));
+        if (mode == 0) return __ldg(reinterpret_cast<const float2*>(p));
         if (mode == 2)
             asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;"
                          : "=f"(v.x), "=f"(v.y)
@@ -118,7 +118,7 @@ template <> struct Vec<4> {
     using T = float4;
     __device__ static T load(const float* p, uint64_t pol, int mode) {
         float4 v;
-        if (mode == 1) return __ldg(reinterpret_cast<const float4*>(p));
+        if (mode == 0) return __ldg(reinterpret_cast<const float4*>(p));
         if (mode == 2)
             asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
                          : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)

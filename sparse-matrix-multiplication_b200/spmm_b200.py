@@ -37,6 +37,7 @@ EXPORTS = [
     "spmm_bsr16_algo", "spmm_device_error", "spmm_hybrid_default_threshold", "spmm_hybrid_choose",
     "spmm_backend_name", "spmm_hybrid_run", "spmm_gpu_count", "spmm_multigpu_run", "spmm_unified_run",
     "spmm_csr_f32_noalloc", "spmm_csr_to_bsr16_device_count", "spmm_csr_to_bsr16_device_fill",
+    "spmm_csr_plan_create", "spmm_csr_plan_execute", "spmm_csr_plan_info", "spmm_csr_plan_destroy",
 ]
 
 
@@ -134,6 +135,10 @@ def lib() -> C.CDLL:
         "spmm_csr_f32_noalloc": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, vp]),
         "spmm_csr_to_bsr16_device_count": (C.c_int, [C.POINTER(CsrView), vp, C.POINTER(i32), vp]),
         "spmm_csr_to_bsr16_device_fill": (C.c_int, [C.POINTER(CsrView), vp, vp, vp, i32, vp]),
+        "spmm_csr_plan_create": (C.c_int, [C.POINTER(CsrView), i32, C.POINTER(CsrTuning), vp, C.POINTER(vp)]),
+        "spmm_csr_plan_execute": (C.c_int, [vp, vp, vp, vp]),
+        "spmm_csr_plan_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_size_t)]),
+        "spmm_csr_plan_destroy": (None, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -360,6 +365,35 @@ def convert_f32(src, dst, n: int, dtype: int = DTYPE_F16, stream=None) -> None:
 
 def bsr16(A: BsrView, B16, Cout, N: int, algo: int = 0, stream=None) -> None:
     check(lib().spmm_bsr16_algo(C.byref(A), ptr(B16), ptr(Cout), N, algo, stream_ptr(stream)), "spmm_bsr16")
+
+
+class CsrPlan:
+    """spmm_csr_plan_* wrapper: inspect A once, execute many times (no allocation per call)."""
+
+    def __init__(self, A: CsrView, N: int, tuning: CsrTuning | None = None, stream=None):
+        self._A = A  # keep the view alive: the plan refers to the same device arrays
+        self.N = N
+        h = C.c_void_p()
+        t = C.byref(tuning) if tuning is not None else None
+        check(lib().spmm_csr_plan_create(C.byref(A), N, t, stream_ptr(stream), C.byref(h)), "spmm_csr_plan_create")
+        self._h = h
+        algo, mx, ws = C.c_int32(), C.c_int32(), C.c_size_t()
+        check(lib().spmm_csr_plan_info(h, C.byref(algo), C.byref(mx), C.byref(ws)), "spmm_csr_plan_info")
+        self.algo, self.max_row, self.ws_bytes = int(algo.value), int(mx.value), int(ws.value)
+
+    def execute(self, B, Cout, stream=None) -> None:
+        check(lib().spmm_csr_plan_execute(self._h, ptr(B), ptr(Cout), stream_ptr(stream)), "spmm_csr_plan_execute")
+
+    def close(self) -> None:
+        if self._h:
+            lib().spmm_csr_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
 
 
 def csr_to_bsr16_device(A: CsrView, dtype: int = DTYPE_F16, stream=None):

@@ -1,0 +1,133 @@
+#!/usr/bin/env python3
+"""B200 pattern x size sweep of the SpMM engine (the B200 counterpart of the reference's
+scripts/run_pattern_sweep.py:46-151 and scripts/roofline.py:177-212).
+
+For every case it times the CUDA-core CSR kernel (both work distributions) and the
+tensor-core BSR kernel on the same matrix, records the BSR fill-in, the hybrid rule's choice
+at the given threshold, GFLOP/s = 2*nnz*N/t, and the fraction of the HBM roofline under the
+reference's compulsory-byte model (8*nnz + 4(M+1) + 4*K*N + 4*M*N for CSR; 516*blocks +
+4(block_rows+1) + 2*K*N + 4*M*N for BSR), against the measured B200 peak. The measured
+CSR/TC crossover in fill-in is what the hybrid threshold is set from.
+
+    python sparse-matrix-multiplication_b200/sweep.py --out sweep.csv [--quick] [--n 256]
+
+Times are CUDA-event medians of single launches with a 256 MiB L2 flush in between.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+
+import spmm_b200 as S  # noqa: E402
+import spmm_patterns as SP  # noqa: E402
+
+
+def peak_hbm_gbs() -> float:
+    f = HERE.parent / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(f.read_text())["hbm_gbs"])
+    except (OSError, ValueError, KeyError):
+        return 6650.0
+
+
+def cases(quick: bool):
+    sizes = (4096, 8192) if quick else (1024, 4096, 8192, 16384)
+    for m in sizes:  # the reference's uniform sweep grid (scripts/roofline.py:59-154)
+        for d in (0.05, 0.01, 0.001):
+            if quick and d == 0.05 and m > 4096:
+                continue
+            yield f"uniform_{m}_d{d}", lambda m=m, d=d: S.generate_uniform_csr(m, m, d, 42)
+    for bw in ((2, 8, 41) if quick else (1, 2, 4, 8, 16, 41, 64)):
+        yield f"banded_8192_bw{bw}", lambda bw=bw: SP.host_csr(8192, 8192, SP.banded_arrays(8192, 8192, bw, 42))
+    for blk in ((8, 16, 128) if quick else (4, 8, 12, 16, 32, 64, 128)):
+        yield f"blockdiag_8192_b{blk}", lambda blk=blk: SP.host_csr(8192, 8192, SP.block_diagonal_arrays(8192, 8192, blk, 42))
+    yield "powerlaw_16384", lambda: SP.host_csr(16384, 16384, SP.power_law_arrays(16384, 16384, 164.0, 1.8, 42))
+
+
+def time_ms(torch, fn, reps: int, flush) -> float:
+    fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return float(np.median(ts))
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--out", type=Path, required=True)
+    ap.add_argument("--n", type=int, default=256)
+    ap.add_argument("--reps", type=int, default=15)
+    ap.add_argument("--threshold", type=float, default=0.0, help="hybrid fill-in threshold (0 = library default)")
+    ap.add_argument("--quick", action="store_true")
+    args = ap.parse_args()
+
+    import torch
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    hbm = peak_hbm_gbs()
+    N = args.n
+    fields = ["case", "rows", "cols", "n", "nnz", "fill_in", "block_density", "num_blocks", "hybrid_choice",
+              "csr_merge_ms", "csr_rowwarp_ms", "tc_ms", "csr_gflops", "tc_gflops", "csr_pct_hbm_roofline",
+              "tc_pct_hbm_roofline", "tc_rel_l2_vs_csr", "faster"]
+    with open(args.out, "w", newline="") as fh:
+        w = csv.DictWriter(fh, fieldnames=fields)
+        w.writeheader()
+        for name, make in cases(args.quick):
+            A = make()
+            M, K = A.rows, A.cols
+            Bh = S.generate_dense(K, N, 43)
+            rp, ci, v = (torch.from_numpy(x).to(dev) for x in (A.row_ptr, A.col_idx, A.values))
+            B = torch.from_numpy(Bh).to(dev)
+            C = torch.empty((M, N), device=dev)
+            view = S.device_view(M, K, rp, ci, v)
+            merge = time_ms(torch, lambda: S.csr_f32(view, B, C, N, S.CSR_MERGE, stream), args.reps, flush)
+            rowwarp = time_ms(torch, lambda: S.csr_f32(view, B, C, N, S.CSR_ROWWARP, stream), args.reps, flush)
+            Ccsr = C.clone()
+            bview, keep = S.csr_to_bsr16_device(view, S.DTYPE_F16, stream)
+            B16 = torch.empty((K, N), dtype=torch.float16, device=dev)
+            S.convert_f32(B, B16, K * N, S.DTYPE_F16, stream)
+            tc = time_ms(torch, lambda: S.bsr16(bview, B16, C, N, 0, stream), args.reps, flush)
+            rel = float(torch.linalg.norm(C - Ccsr) / max(float(torch.linalg.norm(Ccsr)), 1e-30))
+            nb = bview.num_blocks
+            plan = S.hybrid_choose(A, N, args.threshold)
+            flops = 2.0 * A.nnz * N
+            csr_ms = min(merge, rowwarp)
+            csr_bytes = 8 * A.nnz + 4 * (M + 1) + 4 * K * N + 4 * M * N
+            tc_bytes = 516 * nb + 4 * ((M + 15) // 16 + 1) + 2 * K * N + 4 * M * N
+            row = {"case": name, "rows": M, "cols": K, "n": N, "nnz": A.nnz,
+                   "fill_in": round(256.0 * nb / max(A.nnz, 1), 4), "block_density": round(plan["block_density"], 5),
+                   "num_blocks": nb, "hybrid_choice": plan["backend_name"], "csr_merge_ms": round(merge, 5),
+                   "csr_rowwarp_ms": round(rowwarp, 5), "tc_ms": round(tc, 5),
+                   "csr_gflops": round(flops / csr_ms / 1e6, 1), "tc_gflops": round(flops / tc / 1e6, 1),
+                   "csr_pct_hbm_roofline": round(100 * csr_bytes / (csr_ms * 1e-3) / 1e9 / hbm, 2),
+                   "tc_pct_hbm_roofline": round(100 * tc_bytes / (tc * 1e-3) / 1e9 / hbm, 2),
+                   "tc_rel_l2_vs_csr": f"{rel:.3e}", "faster": "tc" if tc < csr_ms else "csr"}
+            w.writerow(row)
+            fh.flush()
+            print(json.dumps(row), flush=True)
+            del keep
+    code, detail = S.device_error(0)
+    if code:
+        raise SystemExit(f"device error {code} ({detail})")
+
+
+if __name__ == "__main__":
+    main()

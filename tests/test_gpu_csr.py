@@ -182,6 +182,26 @@ def test_host_buffer_entry_point(cuda):
     assert bits_equal(C2, C)
 
 
+@pytest.mark.parametrize("name,expect_algo", [("c1", S.CSR_ROWWARP), ("c2", S.CSR_ROWWARP), ("c4", S.CSR_MERGE)])
+def test_plan_picks_distribution_and_matches(cuda, name, expect_algo):
+    torch = cuda
+    A, B = K.config(name)
+    N = B.shape[1]
+    rp, ci, v = _dev(torch, A.row_ptr), _dev(torch, A.col_idx), _dev(torch, A.values)
+    view = S.device_view(A.rows, A.cols, rp, ci, v)
+    plan = S.CsrPlan(view, N, stream=torch.cuda.current_stream())
+    assert plan.max_row == int(np.diff(A.row_ptr).max())
+    assert plan.algo == expect_algo
+    Bd = _dev(torch, B)
+    for _ in range(2):
+        Cd = torch.full((A.rows, N), float("nan"), device="cuda")
+        plan.execute(Bd, Cd, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        got = Cd.cpu().numpy()
+        assert_parity(got, A, B, plan.algo)
+    plan.close()
+
+
 def test_config5_full_size_properties(cuda):
     """C5 at its full size (131072^2, ~17.2M nnz, N=256): exact rows on a sample, and a
     size-independent identity for the whole product, C @ x == A @ (B @ x)."""
