@@ -110,6 +110,16 @@ int spmm_generate_uniform_csr(int32_t rows, int32_t cols, float density, int32_t
  * (reference: src/bench/harness.cu:114-120, generate_dense_row_major) */
 int spmm_generate_dense(int32_t rows, int32_t cols, int32_t seed, float* out);
 
+/* Fast uniform CSR generator, NOT bit-compatible with spmm_generate_uniform_csr: each row
+ * draws the gaps between its kept columns from a geometric(density) distribution (so the
+ * expected nnz is rows * cols * density, as for the Bernoulli generator) and its values
+ * from U[-1,1), both from a counter-based stream keyed by (seed, row). Columns are strictly
+ * increasing in each row. The output depends on (rows, cols, density, seed) only, not on
+ * `threads` (0 = all hardware threads). No counterpart in the reference: it exists to make
+ * config-5-sized inputs in well under a second instead of scanning rows*cols words. */
+int spmm_generate_uniform_csr_fast(int32_t rows, int32_t cols, float density, int64_t seed,
+                                   int32_t threads, spmm_csr_host* out);
+
 /* Rows [row_begin, row_end) of a host CSR, row_ptr rebased to 0.
  * (reference: src/csr.h:27-30, csr_row_slice_host; src/csr.cu:105-123) */
 int spmm_csr_row_slice_host(const spmm_csr_view* m, int32_t row_begin, int32_t row_end,

@@ -11,11 +11,13 @@
 //   dense B       src/bench/harness.cu:114-120
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <limits>
+#include <thread>
 #include <vector>
 
 #include "spmm_c.h"
@@ -297,6 +299,70 @@ int spmm_generate_uniform_csr(int32_t rows, int32_t cols, float density, int32_t
 int spmm_generate_dense(int32_t rows, int32_t cols, int32_t seed, float* out) {
     if (rows < 0 || cols < 0 || (!out && rows && cols)) return SPMM_ERR_INVALID_ARG;
     generate_dense_core(static_cast<size_t>(rows) * static_cast<size_t>(cols), seed, out);
+    return SPMM_OK;
+}
+
+int spmm_generate_uniform_csr_fast(int32_t rows, int32_t cols, float density, int64_t seed, int32_t threads,
+                                   spmm_csr_host* out) {
+    if (!out || rows < 0 || cols < 0 || !(density >= 0.f && density <= 1.f)) return SPMM_ERR_INVALID_ARG;
+    const int nthreads = std::max(1, threads > 0 ? threads : static_cast<int>(std::thread::hardware_concurrency()));
+    // Per row: gaps between kept columns are geometric with parameter p, drawn by inversion
+    // from a counter-based stream (SplitMix64 over (seed, row, draw)), so rows are
+    // independent and the result does not depend on the thread count.
+    const double p = density;
+    const double log1mp = p < 1.0 ? std::log1p(-p) : 0.0;
+    auto mix = [](uint64_t z) {
+        z += 0x9e3779b97f4a7c15ull;
+        z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+        z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+        return z ^ (z >> 31);
+    };
+    auto row_walk = [&](int32_t r, auto&& emit) {
+        if (p <= 0.0 || cols == 0) return;
+        uint64_t ctr = mix(static_cast<uint64_t>(seed) ^ mix(static_cast<uint64_t>(r) + 0x51ed27ull));
+        int64_t c = -1;
+        for (;;) {
+            ctr = mix(ctr);
+            if (p >= 1.0) {
+                c += 1;
+            } else {
+                const double u = (static_cast<double>(ctr >> 11) + 0.5) * 0x1.0p-53;  // (0, 1)
+                c += 1 + static_cast<int64_t>(std::floor(std::log(u) / log1mp));
+            }
+            if (c >= cols) return;
+            ctr = mix(ctr);
+            const float v = static_cast<float>((static_cast<double>(ctr >> 40) + 0.5) * 0x1.0p-24) * 2.0f - 1.0f;
+            emit(static_cast<int32_t>(c), v);
+        }
+    };
+    // Pass 1: counts per row (in parallel), pass 2: fill (in parallel).
+    std::vector<int64_t> counts(static_cast<size_t>(rows) + 1, 0);
+    auto run = [&](auto&& body) {
+        std::vector<std::thread> pool;
+        for (int t = 0; t < nthreads; ++t)
+            pool.emplace_back([&, t] {
+                for (int32_t r = t; r < rows; r += nthreads) body(r);
+            });
+        for (auto& th : pool) th.join();
+    };
+    run([&](int32_t r) {
+        int64_t n = 0;
+        row_walk(r, [&](int32_t, float) { ++n; });
+        counts[r + 1] = n;
+    });
+    for (int32_t r = 0; r < rows; ++r) counts[r + 1] += counts[r];
+    if (counts[rows] > std::numeric_limits<int32_t>::max()) return SPMM_ERR_TOO_LARGE;
+    const int32_t nnz = static_cast<int32_t>(counts[rows]);
+    if (!alloc_csr(rows, cols, nnz, out)) return SPMM_ERR_NO_MEMORY;
+    for (int32_t r = 0; r <= rows; ++r) out->row_ptr[r] = static_cast<int32_t>(counts[r]);
+    run([&](int32_t r) {
+        int64_t k = counts[r];
+        row_walk(r, [&](int32_t c, float v) {
+            out->col_idx[k] = c;
+            out->values[k] = v;
+            ++k;
+        });
+    });
     return SPMM_OK;
 }
 

@@ -30,7 +30,7 @@ BACKEND_CSR, BACKEND_TC = 0, 1
 # Every symbol include/spmm_c.h declares (checked by the CPU test suite).
 EXPORTS = [
     "spmm_status_string", "spmm_version", "spmm_csr_host_alloc", "spmm_csr_host_free", "spmm_csr_from_coo_host",
-    "spmm_generate_uniform_csr", "spmm_generate_dense", "spmm_csr_row_slice_host", "spmm_csr_read_binary",
+    "spmm_generate_uniform_csr", "spmm_generate_uniform_csr_fast", "spmm_generate_dense", "spmm_csr_row_slice_host", "spmm_csr_read_binary",
     "spmm_csr_write_binary", "spmm_csr_validate_host", "spmm_csr_to_bsr16_host", "spmm_bsr_host_free",
     "spmm_bsr_compute_stats", "spmm_nnz_balanced_bounds", "spmm_csr_f32", "spmm_csr_f32_workspace_size",
     "spmm_csr_f32_ws", "spmm_csr_f32_chunk", "spmm_csr_f32_host", "spmm_convert_f32", "spmm_bsr16",
@@ -103,6 +103,7 @@ def lib() -> C.CDLL:
         "spmm_csr_host_free": (None, [C.POINTER(CsrHost)]),
         "spmm_csr_from_coo_host": (C.c_int, [i32, i32, i32, vp, vp, vp, C.POINTER(CsrHost)]),
         "spmm_generate_uniform_csr": (C.c_int, [i32, i32, f32, i32, C.POINTER(CsrHost)]),
+        "spmm_generate_uniform_csr_fast": (C.c_int, [i32, i32, f32, C.c_int64, i32, C.POINTER(CsrHost)]),
         "spmm_generate_dense": (C.c_int, [i32, i32, i32, vp]),
         "spmm_csr_row_slice_host": (C.c_int, [C.POINTER(CsrView), i32, i32, C.POINTER(CsrHost)]),
         "spmm_csr_read_binary": (C.c_int, [C.c_char_p, C.POINTER(CsrHost)]),
@@ -212,6 +213,14 @@ def _adopt(h: CsrHost) -> HostCSR:
 def generate_uniform_csr(rows: int, cols: int, density: float, seed: int) -> HostCSR:
     h = CsrHost()
     check(lib().spmm_generate_uniform_csr(rows, cols, density, seed, C.byref(h)), "spmm_generate_uniform_csr")
+    return _adopt(h)
+
+
+def generate_uniform_csr_fast(rows: int, cols: int, density: float, seed: int, threads: int = 0) -> HostCSR:
+    """Geometric-gap uniform CSR (not the reference's mt19937 stream; same expected nnz)."""
+    h = CsrHost()
+    check(lib().spmm_generate_uniform_csr_fast(rows, cols, density, seed, threads, C.byref(h)),
+          "spmm_generate_uniform_csr_fast")
     return _adopt(h)
 
 

@@ -75,6 +75,61 @@ def test_generator_rejects_bad_density():
         assert e.value.status == -1
 
 
+@pytest.mark.parametrize("rows,cols,d", [(4096, 4096, 0.01), (2000, 300, 0.3), (50, 100000, 0.001), (64, 64, 1.0),
+                                         (10, 20, 0.0), (3, 0, 0.5), (0, 10, 0.5)])
+def test_fast_generator_structure_and_thread_independence(rows, cols, d):
+    a = S.generate_uniform_csr_fast(rows, cols, d, 1234, threads=1)
+    b = S.generate_uniform_csr_fast(rows, cols, d, 1234, threads=7)
+    assert np.array_equal(a.row_ptr, b.row_ptr) and np.array_equal(a.col_idx, b.col_idx)
+    assert np.array_equal(a.values.view(np.uint32), b.values.view(np.uint32))
+    assert a.row_ptr[0] == 0 and np.all(np.diff(a.row_ptr) >= 0) and a.row_ptr[-1] == a.nnz
+    if a.nnz:
+        assert a.col_idx.min() >= 0 and a.col_idx.max() < cols
+        assert np.all(a.values >= -1.0) and np.all(a.values < 1.0)
+        rows_of = np.repeat(np.arange(rows), np.diff(a.row_ptr))
+        same_row = rows_of[1:] == rows_of[:-1]
+        assert np.all(np.diff(a.col_idx)[same_row] > 0), "columns strictly increase inside a row"
+    mean = rows * cols * d
+    sd = np.sqrt(rows * cols * d * (1 - d))
+    assert abs(a.nnz - mean) <= 6 * sd + 1e-9
+    if d == 1.0:
+        assert a.nnz == rows * cols
+
+
+def test_fast_generator_is_uniform_and_seeded():
+    a = S.generate_uniform_csr_fast(8192, 8192, 0.005, 99)
+    # Column and row occupancy: chi-square over 64 equal buckets, far from the 1e-6 tail.
+    for idx, n in ((a.col_idx, 8192), (np.repeat(np.arange(8192), np.diff(a.row_ptr)), 8192)):
+        counts = np.bincount(idx * 64 // n, minlength=64)
+        exp = a.nnz / 64
+        chi2 = float(((counts - exp) ** 2 / exp).sum())
+        assert chi2 < 140, chi2  # 63 d.o.f.: P(chi2 > 140) < 1e-7
+    # Row lengths follow Binomial(cols, d): mean and variance.
+    lens = np.diff(a.row_ptr)
+    assert abs(lens.mean() - 8192 * 0.005) < 0.3
+    assert abs(lens.var() / (8192 * 0.005 * 0.995) - 1) < 0.1
+    # Values U[-1,1): mean ~0, variance ~1/3.
+    assert abs(a.values.mean()) < 0.01 and abs(a.values.var() - 1 / 3) < 0.01
+    c = S.generate_uniform_csr_fast(8192, 8192, 0.005, 100)
+    assert c.nnz != a.nnz or not np.array_equal(c.col_idx, a.col_idx)
+
+
+def test_fast_generator_config5_size_quickly():
+    import time
+    t = time.perf_counter()
+    a = S.generate_uniform_csr_fast(131072, 131072, 0.001, 42)
+    dt = time.perf_counter() - t
+    assert abs(a.nnz - 17179869) < 6 * np.sqrt(17179869)
+    assert dt < 30, dt
+
+
+def test_fast_generator_rejects_bad_density():
+    for d in (-0.1, 1.5, float("nan")):
+        with pytest.raises(S.SpmmError) as e:
+            S.generate_uniform_csr_fast(10, 10, d, 1)
+        assert e.value.status == -1
+
+
 def test_dense_bit_identical():
     for r, c, s in [(4096, 64, 43), (123, 45, 9), (1, 1, 0)]:
         assert np.array_equal(S.generate_dense(r, c, s).view(np.uint32), O.gen_dense(r, c, s).view(np.uint32))
