@@ -78,6 +78,19 @@ def test_ragged_shapes(cuda, M, Kc, N, algo):
     check_bsr(run_bsr(cuda, Hb, B16, N, algo=algo), Hb, B16, S.DTYPE_F16)
 
 
+@pytest.mark.parametrize("M,Kc,N", [(32768, 512, 128), (20000, 333, 136)])
+def test_eight_block_rows_per_cta(cuda, M, Kc, N):
+    # Enough block-rows that the launcher groups eight per CTA (>= one CTA per SM at G=8),
+    # with skewed rows so the producer merges lists of very different lengths.
+    lens = np.random.default_rng(M).integers(0, 12, size=M)
+    lens[::97] = np.minimum(Kc, 300)
+    A = K.random_csr(M, Kc, lens, seed=5)
+    Hb = S.csr_to_bsr16(A)
+    assert (Hb.block_rows + 7) // 8 * ((N + 127) // 128) >= 148
+    B16 = O.to_half_bits(K.dense(Kc, N, 6))
+    check_bsr(run_bsr(cuda, Hb, B16, N, algo=1), Hb, B16, S.DTYPE_F16)
+
+
 def test_empty_block_rows_and_uniform_fill(cuda):
     # Uniform sparsity (high fill-in) with whole empty block-rows in between.
     lens = np.random.default_rng(1).integers(0, 30, size=512)
