@@ -147,6 +147,37 @@ class Clocks:
 # ------------------------------------------------------------------------ CPU baseline
 
 
+def gather_ceiling(torch, Bd, rows: int, fetches: int, stream) -> float | None:
+    """Random whole-row gather rate (GB/s) of this GPU over the first `rows` rows of Bd
+    (N = 256 only): lib/libspmm_probe.so, same residency and load width as the CSR kernels,
+    no arithmetic. The median of 5 launches of `fetches` 1 KB rows each."""
+    import ctypes as C
+
+    so = PKG / "lib" / "libspmm_probe.so"
+    if Bd.shape[1] != 256 or not so.exists() or fetches < 4:
+        return None
+    lib = C.CDLL(str(so))
+    lib.spmm_probe_gather.argtypes = [C.c_void_p, C.c_uint32, C.c_longlong, C.c_uint32, C.c_void_p, C.c_void_p]
+    ctas = C.c_int()
+    if lib.spmm_probe_ctas(C.byref(ctas)) != 0:
+        return None
+    out = torch.empty(ctas.value * 256, dtype=torch.float32, device=Bd.device)
+    fetches -= fetches % 4
+    ts = []
+    for i in range(7):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        rc = lib.spmm_probe_gather(C.c_void_p(Bd.data_ptr()), rows, fetches, i, C.c_void_p(out.data_ptr()),
+                                   C.c_void_p(stream.cuda_stream))
+        b.record()
+        torch.cuda.synchronize()
+        if rc != 0:
+            return None
+        if i >= 2:
+            ts.append(a.elapsed_time(b))
+    return fetches * 1024.0 / (statistics.median(ts) * 1e-3) / 1e9
+
+
 def cpu_baseline_run(A, B, steps: int, warmup: int):
     """The reference's CSR x dense semantics on all host cores (oracle port)."""
     from oracle import oracle as O
@@ -263,12 +294,15 @@ def main():
         def step():
             S.bsr16(bview, B16, Cd, N, 0, stream)
 
+        launches = 1
+
         alg_bytes = 512 * Ah.num_blocks + 4 * Ah.num_blocks + 4 * (Ah.block_rows + 1) + 2 * A.cols * N + 4 * A.rows * N
         kernel_name = "bsr_tcgen05_kernel"
     else:
         # Inspect the rank's rows once (picks the work distribution, owns the workspace).
         plan = S.CsrPlan(view, N, stream=stream)
         csr_algo = plan.algo
+        launches = plan.k_phases  # kernel launches per step
 
         def step():
             plan.execute(Bd, Cd, stream)
@@ -319,7 +353,42 @@ def main():
 
     # ---- end to end through the host-buffer entry point
     e2e = None
-    if not args.no_e2e and cfg_name != "c3":
+    if not args.no_e2e and cfg_name != "c3" and world > 1:
+        # Multi-GPU end to end, the spmm_multigpu data flow: every rank copies its A rows
+        # host -> device, rank 0 copies B once and broadcasts it over NVLink (NCCL), every
+        # rank runs its plan (spmm_csr_plan_execute) and copies its C rows back.
+        pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
+        h_rp, h_ci, h_va = pin(Ar.row_ptr), pin(Ar.col_idx), pin(Ar.values)
+        h_b = pin(Bh) if rank == 0 else None
+        h_c = torch.empty((max(rows_r, 1), N), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            rp.copy_(h_rp, non_blocking=True)
+            ci.copy_(h_ci, non_blocking=True)
+            va.copy_(h_va, non_blocking=True)
+            if rank == 0:
+                Bd.copy_(h_b, non_blocking=True)
+            dist.broadcast(Bd, src=0)
+            plan.execute(Bd, Cd, stream)
+            h_c.copy_(Cd, non_blocking=True)
+            torch.cuda.synchronize()
+
+        for _ in range(2):
+            e2e_step()
+        ke = max(3, min(K, 20))
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(ke):
+            e2e_step()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / ke
+        barrier()
+        e2e_ms = max_over_ranks(e2e_ms)
+        h2d = sum_over_ranks(float(Ar.row_ptr.nbytes + Ar.col_idx.nbytes + Ar.values.nbytes)) + Bh.nbytes
+        d2h = sum_over_ranks(float(rows_r * N * 4))
+        e2e = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "api": "per rank: A rows H2D, B H2D on rank 0 + NCCL broadcast, spmm_csr_plan_execute, C rows D2H"}
+    elif not args.no_e2e and cfg_name != "c3":
         pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
         hA = S.HostCSR(Ar.rows, Ar.cols, pin(Ar.row_ptr).numpy(), pin(Ar.col_idx).numpy(), pin(Ar.values).numpy())
         hB = pin(Bh).numpy()
@@ -363,7 +432,18 @@ def main():
                               "frac": round(tflops / tc_peak, 4)}
     else:
         gathered = 4.0 * Ar.nnz * N  # B-row bytes the gather moves through L2 per launch
-        roofline["l2_gather_gbs"] = round(gathered / (avg_launch_ms * 1e-3) / 1e9, 1)
+        gather_gbs = gathered / (avg_launch_ms * 1e-3) / 1e9
+        roofline["l2_gather_gbs"] = round(gather_gbs, 1)
+        # The ceiling that actually bounds a uniform gather: whole random B rows pulled into
+        # the SMs, measured by a load-only probe over B's own footprint and over an L2-resident
+        # 32 MB part of it.
+        same = gather_ceiling(torch, Bd, A.cols, Ar.nnz, stream)
+        resident = gather_ceiling(torch, Bd, min(A.cols, 32768), Ar.nnz, stream)
+        if same:
+            roofline["gather_ceiling"] = {
+                "achieved_gbs": round(gather_gbs, 1), "ceiling_gbs": round(same, 1),
+                "frac": round(gather_gbs / same, 4), "l2_resident_ceiling_gbs": round(resident or 0.0, 1),
+                "probe": "random 1 KB B-row fetches over B's footprint, load-only (lib/libspmm_probe.so)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -382,7 +462,7 @@ def main():
                        "kernel": kernel_name,
                        "l2": "inputs larger than L2" if not small else "L2 flushed between steps",
                        "b_broadcast_ms": round(bcast_ms, 4)},
-            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": K,
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": K * launches,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -175,12 +175,17 @@ int spmm_nnz_balanced_bounds(const int32_t* row_ptr, int32_t rows, int64_t nnz, 
  * column slab (the grid walks N slab by slab so a slab's B columns stay in L2): 0 = auto,
  * else 32/64/128/256. b_policy: 0 = plain non-coherent B loads (default; measured fastest
  * on B200 in an interleaved A/B over configs 1, 2, 4, 5), 1 = with an L2 evict-last hint,
- * 2 = evict-last and no L1 allocation. */
+ * 2 = evict-last and no L1 allocation. k_phases (SPMM_CSR_ROWWARP only; 0 = auto): cut
+ * A's columns into this many equal ranges and run one launch per range in order, each
+ * continuing every C element's FMA chain from the value the previous launch left in C, so
+ * only 1/k_phases of B has to stay L2-resident at a time (1..8; direct calls take 0 as 1,
+ * plans choose). Results are bit-identical for every k_phases. */
 typedef struct spmm_csr_tuning {
     int32_t chunk;
     int32_t col_pass;
     int32_t b_policy;
-    int32_t reserved[5];
+    int32_t k_phases;
+    int32_t reserved[4];
 } spmm_csr_tuning;
 
 /* C = A * B, FP32, on `stream`; A, B, C are device pointers. Asynchronous.
@@ -236,6 +241,8 @@ int spmm_csr_plan_create(const spmm_csr_view* A, int32_t N, const spmm_csr_tunin
                          spmm_csr_plan** plan);
 int spmm_csr_plan_execute(const spmm_csr_plan* plan, const float* B, float* C, void* stream);
 int spmm_csr_plan_info(const spmm_csr_plan* plan, int32_t* algo, int32_t* max_row, size_t* ws_bytes);
+/* Number of column phases the plan runs (kernel launches per spmm_csr_plan_execute). */
+int spmm_csr_plan_k_phases(const spmm_csr_plan* plan, int32_t* k_phases);
 void spmm_csr_plan_destroy(spmm_csr_plan* plan);
 
 /* End-to-end call on HOST buffers: copies A and B to the current device (pinned or

@@ -71,4 +71,15 @@ int ensure_device_buffer(void** buf, size_t* cur, size_t bytes, bool zero, cudaS
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// FP32 CSR launcher shared by every entry point (csr_kernels.cu). `ksplit_ready`: the first
+// (k_phases - 1) * M ints of `ws` already hold the column-phase split positions (plans).
+int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
+                   const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream, DeviceState* st,
+                   bool ksplit_ready = false);
+int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, const spmm_csr_tuning* tune,
+                            int sm_count, size_t* bytes);
+size_t csr_f32_counter_bytes(const spmm_csr_view* A, int32_t N, const spmm_csr_tuning* tune, int sm_count);
+int csr_f32_chunk(const spmm_csr_view* A, const spmm_csr_tuning* tune, int sm_count);
+int csr_f32_ksplit(const spmm_csr_view* A, int phases, int* split, cudaStream_t stream, DeviceState* st);
+
 }  // namespace spmm_b200

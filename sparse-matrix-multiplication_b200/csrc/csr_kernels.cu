@@ -66,6 +66,10 @@ struct CsrArgs {
     int* counters;       // num_chunks per slab, all-zero between calls
     float* partials;     // num_chunks * 2 * N
     int b_policy;        // B loads: 0 plain, 1 L2 evict-last, 2 evict-last + no L1 allocation
+    // Column phases (ROWWARP): launch `phase` of `phases` runs positions [split[phase-1][i],
+    // split[phase][i]) of row i (split[-1] = row start, split[phases-1] = row end).
+    int phase, phases;
+    int* ksplit;         // (phases - 1) x M split positions
     DeviceErrorRecord* err;
 };
 
@@ -239,6 +243,20 @@ __device__ __forceinline__ void store_slab(const CsrArgs& a, float* dst, int col
 }
 
 template <int VEC, int R>
+__device__ __forceinline__ void load_slab(const CsrArgs& a, const float* src, int col0, int lane,
+                                          float (&acc)[R][VEC]) {
+    using V = Vec<VEC>;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int c = lane_col<VEC>(col0, r, lane);
+        typename V::T t{};
+        if (c < a.N) t = V::loadcg(src + c);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[r][e] = V::get(t, e);
+    }
+}
+
+template <int VEC, int R>
 __device__ __forceinline__ void zero(float (&acc)[R][VEC]) {
 #pragma unroll
     for (int r = 0; r < R; ++r)
@@ -256,7 +274,7 @@ __device__ __forceinline__ void row_bounds(const CsrArgs& a, int i, int& rs, int
         record_device_error(a.err, SPMM_ERR_BAD_INDEX, -1 - static_cast<long long>(i));
 }
 
-template <int VEC, int R, int U>
+template <int VEC, int R, int U, bool PHASED>
 __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kernel(CsrArgs a) {
     constexpr int W = 32 * VEC * R;
     const int lane = threadIdx.x & 31;
@@ -268,9 +286,49 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kerne
         int rs, re;
         row_bounds(a, i, rs, re);
         float acc[R][VEC];
-        zero(acc);
-        accumulate<VEC, R, U>(a, rs, re, col0, lane, pol, acc);
-        store_slab<VEC, R>(a, a.C + static_cast<size_t>(i) * a.N, col0, lane, acc, true);
+        float* crow = a.C + static_cast<size_t>(i) * a.N;
+        if constexpr (PHASED) {
+            // This phase's positions of row i; the chain continues from the value the
+            // previous phase stored in C (phase 0 starts from +0 and writes every row).
+            int lo = rs, hi = re;
+            if (a.phase > 0) lo = clampi(__ldcg(a.ksplit + static_cast<size_t>(a.phase - 1) * a.M + i), rs, re);
+            if (a.phase < a.phases - 1) hi = clampi(__ldcg(a.ksplit + static_cast<size_t>(a.phase) * a.M + i), lo, re);
+            if (a.phase > 0 && lo == hi) continue;
+            if (a.phase > 0) load_slab<VEC, R>(a, crow, col0, lane, acc);
+            else zero(acc);
+            accumulate<VEC, R, U>(a, lo, hi, col0, lane, pol, acc);
+        } else {
+            zero(acc);
+            accumulate<VEC, R, U>(a, rs, re, col0, lane, pol, acc);
+        }
+        store_slab<VEC, R>(a, crow, col0, lane, acc, true);
+    }
+}
+
+// Split positions for column phases: split[b][i] = row start + number of row-i nonzeros with
+// column < K * (b + 1) / phases. Any monotone cut of a row's positions gives the same FMA
+// chain, so the results do not depend on these values; sorted rows make each phase touch
+// only its range of B rows.
+__global__ void __launch_bounds__(kThreads) csr_ksplit_kernel(CsrArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int warp = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+    const int nwarps = gridDim.x * kWarpsPerCta;
+    const int nb = a.phases - 1;  // <= 7
+    for (int i = warp; i < a.M; i += nwarps) {
+        int rs, re;
+        row_bounds(a, i, rs, re);
+        int mine = 0;  // lane b < nb counts columns below boundary b
+        for (int base = rs; base < re; base += 32) {
+            const int p = base + lane;
+            const int k = p < re ? __ldcs(a.col_idx + p) : 0x7fffffff;
+#pragma unroll 1
+            for (int b = 0; b < nb; ++b) {
+                const long long kb = static_cast<long long>(a.K) * (b + 1) / a.phases;
+                const int n = __popc(__ballot_sync(kFull, p < re && static_cast<long long>(k) < kb));
+                if (lane == b) mine += n;
+            }
+        }
+        if (lane < nb) a.ksplit[static_cast<size_t>(lane) * a.M + i] = rs + mine;
     }
 }
 
@@ -410,6 +468,10 @@ struct Geometry {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+constexpr int kMaxPhases = 8;
+
 // Slab width: the narrowest of 32/64/128/256 columns that covers N, at most 256. Narrower
 // slabs that keep a slab's B columns L2-resident (col_pass) re-read A once per slab; on B200
 // at config 5 (B = 134 MB) one 256-wide slab with evict-last B loads measured faster than two
@@ -478,10 +540,17 @@ int check_tune(const spmm_csr_tuning* tune) {
         tune->col_pass != 256)
         return SPMM_ERR_INVALID_ARG;
     if (tune->b_policy < 0 || tune->b_policy > 2) return SPMM_ERR_INVALID_ARG;
+    if (tune->k_phases < 0 || tune->k_phases > kMaxPhases) return SPMM_ERR_INVALID_ARG;
     return SPMM_OK;
 }
 
-size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+int resolve_phases(int algo, const spmm_csr_tuning* tune) {
+    return (algo == SPMM_CSR_ROWWARP && tune && tune->k_phases > 1) ? tune->k_phases : 1;
+}
+
+size_t ksplit_bytes(int phases, int M) {
+    return phases > 1 ? align_up(static_cast<size_t>(phases - 1) * static_cast<size_t>(M) * sizeof(int), 256) : 0;
+}
 
 // Counters for every slab the narrowest slab width (32 columns) could need, so the size does
 // not depend on the operands' alignment.
@@ -498,8 +567,12 @@ template <int VEC, int R>
 void launch_vr(int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
     // Eight vector loads per lane in flight: U nonzeros x R strides.
     constexpr int U = (8 / R) > 0 ? (8 / R) : 1;
-    if (algo == SPMM_CSR_ROWWARP) csr_rowwarp_kernel<VEC, R, U><<<grid, kThreads, 0, s>>>(a);
-    else csr_merge_kernel<VEC, R, U><<<grid, kThreads, 0, s>>>(a);
+    if (algo == SPMM_CSR_ROWWARP) {
+        if (a.phases > 1) csr_rowwarp_kernel<VEC, R, U, true><<<grid, kThreads, 0, s>>>(a);
+        else csr_rowwarp_kernel<VEC, R, U, false><<<grid, kThreads, 0, s>>>(a);
+    } else {
+        csr_merge_kernel<VEC, R, U><<<grid, kThreads, 0, s>>>(a);
+    }
 }
 
 void launch(const Geometry& g, int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
@@ -521,7 +594,7 @@ void launch(const Geometry& g, int algo, const CsrArgs& a, dim3 grid, cudaStream
 // Shared by the C entry points below and by the allocation-free variant in noalloc.cu.
 int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
                    const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream,
-                   DeviceState* st) {
+                   DeviceState* st, bool ksplit_ready) {
     SPMM_TRY(check_view(A, B, C, N));
     SPMM_TRY(check_tune(tune));
     if (algo == SPMM_CSR_AUTO) algo = SPMM_CSR_MERGE;
@@ -549,6 +622,24 @@ int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, 
     if (algo == SPMM_CSR_ROWWARP) {
         const long long warps = std::min<long long>(A->rows, static_cast<long long>(st->sm_count) * 64);
         grid.x = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
+        a.phases = resolve_phases(algo, tune);
+        if (a.phases > 1) {
+            // Column phases: split positions (computed here unless the caller holds them),
+            // then one launch per phase, then the workspace is cleared again.
+            const size_t need = ksplit_bytes(a.phases, A->rows);
+            if (need > ws_bytes || !ws) return SPMM_ERR_INVALID_ARG;
+            a.ksplit = static_cast<int*>(ws);
+            if (!ksplit_ready) {
+                csr_ksplit_kernel<<<grid.x, kThreads, 0, stream>>>(a);
+                SPMM_CUDA_TRY(cudaGetLastError());
+            }
+            for (a.phase = 0; a.phase < a.phases; ++a.phase) {
+                launch(g, algo, a, grid, stream);
+                SPMM_CUDA_TRY(cudaGetLastError());
+            }
+            if (!ksplit_ready) SPMM_CUDA_TRY(cudaMemsetAsync(ws, 0, need, stream));
+            return SPMM_OK;
+        }
     } else {
         a.S = resolve_chunk(A, tune, st->sm_count);
         a.items = static_cast<long long>(A->rows) + A->nnz;
@@ -572,11 +663,33 @@ int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, con
     SPMM_TRY(check_tune(tune));
     *bytes = 0;
     if (algo == SPMM_CSR_AUTO) algo = SPMM_CSR_MERGE;
-    if (algo == SPMM_CSR_ROWWARP || A->rows == 0 || N == 0) return SPMM_OK;
+    if (A->rows == 0 || N == 0) return SPMM_OK;
+    if (algo == SPMM_CSR_ROWWARP) {
+        *bytes = ksplit_bytes(resolve_phases(algo, tune), A->rows);
+        return SPMM_OK;
+    }
     if (algo != SPMM_CSR_MERGE) return SPMM_ERR_INVALID_ARG;
     const int S = resolve_chunk(A, tune, sm_count);
     const long long items = static_cast<long long>(A->rows) + A->nnz;
     *bytes = merge_workspace_bytes((items + S - 1) / S, N);
+    return SPMM_OK;
+}
+
+// Split positions for a plan that keeps them across executions.
+int csr_f32_ksplit(const spmm_csr_view* A, int phases, int* split, cudaStream_t stream, DeviceState* st) {
+    if (phases <= 1 || A->rows == 0) return SPMM_OK;
+    CsrArgs a{};
+    a.M = A->rows;
+    a.K = A->cols;
+    a.nnz = A->nnz;
+    a.row_ptr = A->row_ptr;
+    a.col_idx = A->col_idx;
+    a.phases = phases;
+    a.ksplit = split;
+    a.err = st->err;
+    const long long warps = std::min<long long>(A->rows, static_cast<long long>(st->sm_count) * 64);
+    csr_ksplit_kernel<<<static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta), kThreads, 0, stream>>>(a);
+    SPMM_CUDA_TRY(cudaGetLastError());
     return SPMM_OK;
 }
 
@@ -620,7 +733,7 @@ int spmm_csr_f32_ws(const spmm_csr_view* A, const float* B, float* C, int32_t N,
                     const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, void* stream) {
     DeviceState* st = nullptr;
     SPMM_TRY(current_device_state(&st));
-    return csr_f32_launch(A, B, C, N, algo, tune, ws, ws_bytes, as_stream(stream), st);
+    return csr_f32_launch(A, B, C, N, algo, tune, ws, ws_bytes, as_stream(stream), st, false);
 }
 
 int spmm_csr_f32(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo, void* stream) {
@@ -631,7 +744,7 @@ int spmm_csr_f32(const spmm_csr_view* A, const float* B, float* C, int32_t N, in
     SPMM_TRY(csr_f32_workspace_bytes(A, N, algo, nullptr, st->sm_count, &need));
     std::lock_guard<std::mutex> lock(st->mu);
     SPMM_TRY(ensure_device_buffer(&st->csr_ws, &st->csr_ws_bytes, need, true, as_stream(stream)));
-    return csr_f32_launch(A, B, C, N, algo, nullptr, st->csr_ws, st->csr_ws_bytes, as_stream(stream), st);
+    return csr_f32_launch(A, B, C, N, algo, nullptr, st->csr_ws, st->csr_ws_bytes, as_stream(stream), st, false);
 }
 
 }  // extern "C"

@@ -48,10 +48,6 @@ const NcclApi& nccl() {
     return api;
 }
 
-int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
-                   const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream, DeviceState* st);
-int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, const spmm_csr_tuning* tune,
-                            int sm_count, size_t* bytes);
 
 namespace {
 

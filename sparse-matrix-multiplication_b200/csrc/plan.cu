@@ -28,10 +28,6 @@ struct spmm_csr_plan {
 
 namespace spmm_b200 {
 
-int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
-                   const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream, DeviceState* st);
-int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, const spmm_csr_tuning* tune,
-                            int sm_count, size_t* bytes);
 
 namespace {
 
@@ -43,6 +39,18 @@ __global__ void max_row_kernel(const int* __restrict__ row_ptr, int M, int* out)
         best = max(best, __ldg(row_ptr + i + 1) - __ldg(row_ptr + i));
     for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_down_sync(0xffffffffu, best, o));
     if ((threadIdx.x & 31) == 0) atomicMax(out, best);
+}
+
+// Column phases for ROWWARP: enough that each phase's share of B (K / phases rows of N
+// floats) fits in kPhaseL2Share of the L2.
+constexpr double kPhaseL2Share = 0.0;  // 0: phases off unless the caller asks
+
+int auto_phases(const spmm_csr_view* A, int32_t N, const DeviceState* st) {
+    if (kPhaseL2Share <= 0.0 || st->l2_bytes <= 0) return 1;
+    const double b_bytes = 4.0 * A->cols * static_cast<double>(N);
+    const double share = kPhaseL2Share * st->l2_bytes;
+    int ph = static_cast<int>((b_bytes + share - 1) / share);
+    return std::min(std::max(ph, 1), 8);
 }
 
 }  // namespace
@@ -85,12 +93,19 @@ int spmm_csr_plan_create(const spmm_csr_view* A, int32_t N, const spmm_csr_tunin
         const long long fair = items / (static_cast<long long>(st->sm_count) * kResidentWarpsPerSm);
         const long long limit = std::max<long long>(4 * fair, 256);
         p->algo = p->max_row <= limit ? SPMM_CSR_ROWWARP : SPMM_CSR_MERGE;
-        rc = csr_f32_workspace_bytes(A, N, p->algo, tune, st->sm_count, &p->ws_bytes);
+        if (p->algo == SPMM_CSR_ROWWARP) {
+            if (p->tune.k_phases <= 0) p->tune.k_phases = auto_phases(A, N, st);
+        } else {
+            p->tune.k_phases = 0;
+        }
+        rc = csr_f32_workspace_bytes(A, N, p->algo, &p->tune, st->sm_count, &p->ws_bytes);
     }
     if (rc == SPMM_OK && p->ws_bytes) {
         if (cudaMalloc(&p->ws, p->ws_bytes) != cudaSuccess) rc = SPMM_ERR_NO_MEMORY;
-        else if (cudaMemsetAsync(p->ws, 0, p->ws_bytes, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
-            rc = SPMM_ERR_CUDA;
+        else if (cudaMemsetAsync(p->ws, 0, p->ws_bytes, s) != cudaSuccess) rc = SPMM_ERR_CUDA;
+        else if (p->algo == SPMM_CSR_ROWWARP)
+            rc = csr_f32_ksplit(&p->A, p->tune.k_phases, static_cast<int*>(p->ws), s, st);
+        if (rc == SPMM_OK && cudaStreamSynchronize(s) != cudaSuccess) rc = SPMM_ERR_CUDA;
     }
     if (rc != SPMM_OK) {
         cudaFree(p->ws);
@@ -106,7 +121,13 @@ int spmm_csr_plan_execute(const spmm_csr_plan* p, const float* B, float* C, void
     DeviceState* st = nullptr;
     SPMM_TRY(current_device_state(&st));
     if (st->device != p->device) return SPMM_ERR_INVALID_ARG;
-    return csr_f32_launch(&p->A, B, C, p->N, p->algo, &p->tune, p->ws, p->ws_bytes, as_stream(stream), st);
+    return csr_f32_launch(&p->A, B, C, p->N, p->algo, &p->tune, p->ws, p->ws_bytes, as_stream(stream), st, true);
+}
+
+int spmm_csr_plan_k_phases(const spmm_csr_plan* p, int32_t* k_phases) {
+    if (!p || !k_phases) return SPMM_ERR_INVALID_ARG;
+    *k_phases = p->algo == SPMM_CSR_ROWWARP ? std::max(1, p->tune.k_phases) : 1;
+    return SPMM_OK;
 }
 
 int spmm_csr_plan_info(const spmm_csr_plan* p, int32_t* algo, int32_t* max_row, size_t* ws_bytes) {

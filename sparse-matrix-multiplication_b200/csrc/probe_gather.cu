@@ -1,0 +1,83 @@
+// Measurement helper for bench.py (lib/libspmm_probe.so, not part of the SpMM C ABI): the
+// random-row gather ceiling of this GPU, i.e. how fast SMs can pull whole rows of a dense
+// FP32 row-major matrix from the memory system when the rows are picked at random.
+//
+// The FP32 CSR kernels move one full B row (4 * N bytes) per nonzero; with uniformly random
+// columns nothing is reused in L1, so the rate at which whole random rows reach the SMs bounds
+// them, not HBM. This kernel does only that: same residency as the CSR kernels (4 CTAs x 8
+// warps per SM), one warp per row fetch, each lane two 16-byte loads of a 256-float row,
+// eight loads per lane in flight, rows picked by a counter hash over a buffer of `rows` rows
+// (choose a footprint inside L2 for the L2 ceiling, or the real B's size). The loaded values
+// are summed and one float per thread is stored so that nothing is optimised away.
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    return x;
+}
+
+__global__ void __launch_bounds__(kThreads, 4) gather_probe_kernel(const float* __restrict__ buf, uint32_t rows,
+                                                                   long long fetches, uint32_t seed,
+                                                                   float* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const long long nwarps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    constexpr int U = 4;
+    long long f = warp * U;
+    for (; f + U <= fetches; f += nwarps * U) {
+        float4 b[U][2];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint32_t h = mix32(static_cast<uint32_t>(f + u) * 0x9e3779b9u + seed);
+            const uint32_t r = static_cast<uint32_t>((static_cast<uint64_t>(h) * rows) >> 32);
+            const float4* row = reinterpret_cast<const float4*>(buf + static_cast<size_t>(r) * 256);
+            b[u][0] = __ldg(row + lane);
+            b[u][1] = __ldg(row + 32 + lane);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            s0 += b[u][0].x + b[u][1].x;
+            s1 += b[u][0].y + b[u][1].y;
+            s2 += b[u][0].z + b[u][1].z;
+            s3 += b[u][0].w + b[u][1].w;
+        }
+    }
+    out[static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x] = s0 + s1 + s2 + s3;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Fetch `fetches` random 1 KB rows (256 floats) of `buf` (rows x 256, 16-byte aligned) on
+// `stream`. `out` needs grid_ctas * 256 floats, grid_ctas = sm_count * 4 (see spmm_probe_ctas).
+// Returns 0, or a cudaError_t value.
+int spmm_probe_ctas(int* ctas) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 1;
+    *ctas = sms * 4;
+    return 0;
+}
+
+int spmm_probe_gather(const float* buf, uint32_t rows, long long fetches, uint32_t seed, float* out, void* stream) {
+    if (!buf || !out || rows == 0 || fetches < 0 || (reinterpret_cast<uintptr_t>(buf) & 15)) return 1;
+    int ctas = 0;
+    if (spmm_probe_ctas(&ctas)) return 1;
+    gather_probe_kernel<<<ctas, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(buf, rows, fetches, seed, out);
+    return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -38,6 +38,7 @@ EXPORTS = [
     "spmm_backend_name", "spmm_hybrid_run", "spmm_gpu_count", "spmm_multigpu_run", "spmm_unified_run",
     "spmm_csr_f32_noalloc", "spmm_csr_to_bsr16_device_count", "spmm_csr_to_bsr16_device_fill",
     "spmm_csr_plan_create", "spmm_csr_plan_execute", "spmm_csr_plan_info", "spmm_csr_plan_destroy",
+    "spmm_csr_plan_k_phases",
 ]
 
 
@@ -76,7 +77,8 @@ class BsrStats(C.Structure):
 
 
 class CsrTuning(C.Structure):
-    _fields_ = [("chunk", C.c_int32), ("col_pass", C.c_int32), ("b_policy", C.c_int32), ("reserved", C.c_int32 * 5)]
+    _fields_ = [("chunk", C.c_int32), ("col_pass", C.c_int32), ("b_policy", C.c_int32), ("k_phases", C.c_int32),
+                ("reserved", C.c_int32 * 4)]
 
 
 class HybridPlan(C.Structure):
@@ -139,6 +141,7 @@ def lib() -> C.CDLL:
         "spmm_csr_plan_create": (C.c_int, [C.POINTER(CsrView), i32, C.POINTER(CsrTuning), vp, C.POINTER(vp)]),
         "spmm_csr_plan_execute": (C.c_int, [vp, vp, vp, vp]),
         "spmm_csr_plan_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_size_t)]),
+        "spmm_csr_plan_k_phases": (C.c_int, [vp, C.POINTER(i32)]),
         "spmm_csr_plan_destroy": (None, [vp]),
     }
     for name, (res, args) in sig.items():
@@ -389,6 +392,9 @@ class CsrPlan:
         algo, mx, ws = C.c_int32(), C.c_int32(), C.c_size_t()
         check(lib().spmm_csr_plan_info(h, C.byref(algo), C.byref(mx), C.byref(ws)), "spmm_csr_plan_info")
         self.algo, self.max_row, self.ws_bytes = int(algo.value), int(mx.value), int(ws.value)
+        ph = C.c_int32()
+        check(lib().spmm_csr_plan_k_phases(h, C.byref(ph)), "spmm_csr_plan_k_phases")
+        self.k_phases = int(ph.value)  # kernel launches per execute
 
     def execute(self, B, Cout, stream=None) -> None:
         check(lib().spmm_csr_plan_execute(self._h, ptr(B), ptr(Cout), stream_ptr(stream)), "spmm_csr_plan_execute")

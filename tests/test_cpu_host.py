@@ -37,6 +37,15 @@ def test_c_abi_exports_every_declared_symbol():
     assert sorted(S.EXPORTS) == names
 
 
+def test_probe_library_loads_and_exports():
+    import ctypes
+
+    so = S.LIB_PATH.parent / "libspmm_probe.so"
+    L = ctypes.CDLL(str(so))
+    for n in ("spmm_probe_ctas", "spmm_probe_gather"):
+        assert hasattr(L, n)
+
+
 def test_cxx_api_library_exports_reference_symbols():
     out = subprocess.run(["nm", "-DC", "--defined-only", str(S.CXX_LIB_PATH)], capture_output=True, text=True,
                          check=True).stdout

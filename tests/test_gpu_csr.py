@@ -202,6 +202,71 @@ def test_plan_picks_distribution_and_matches(cuda, name, expect_algo):
     plan.close()
 
 
+@pytest.mark.parametrize("phases", [2, 3, 5, 8])
+@pytest.mark.parametrize("N", [64, 100, 257])
+def test_column_phases_bit_exact(cuda, phases, N):
+    # ROWWARP in column phases: each launch continues every element's chain from C, so the
+    # result is the one sequential chain; empty phases, rows empty in every phase and N > 256
+    # (two slabs per phase) included. The workspace is all-zero again afterwards.
+    rng = np.random.default_rng(phases * 1000 + N)
+    lens = rng.integers(0, 60, size=900)
+    lens[::50] = 0
+    lens[7] = 700
+    A = K.random_csr(900, 3000, lens, seed=N)
+    B = K.dense(3000, N, phases)
+    t = S.CsrTuning(k_phases=phases)
+    torch = cuda
+    rp, ci, v = _dev(torch, A.row_ptr), _dev(torch, A.col_idx), _dev(torch, A.values)
+    view = S.device_view(A.rows, A.cols, rp, ci, v)
+    n = S.csr_workspace_size(view, N, S.CSR_ROWWARP, t)
+    assert n >= 4 * (phases - 1) * A.rows
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    Bd = _dev(torch, B)
+    for _ in range(2):
+        Cd = torch.full((A.rows, N), float("nan"), device="cuda")
+        S.csr_f32_ws(view, Bd, Cd, N, S.CSR_ROWWARP, t, ws, n, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        assert int(ws.count_nonzero()) == 0
+        assert_parity(Cd.cpu().numpy(), A, B, S.CSR_ROWWARP)
+
+
+def test_column_phases_unsorted_rows_keep_stored_order(cuda):
+    # Columns shuffled inside each row (and duplicated): the phases cut positions, not column
+    # values, so the chain still runs in stored order.
+    A = K.random_csr(400, 2000, np.random.default_rng(3).integers(0, 80, size=400), seed=4)
+    rng = np.random.default_rng(5)
+    ci = A.col_idx.copy()
+    for r in range(A.rows):
+        s, e = A.row_ptr[r], A.row_ptr[r + 1]
+        ci[s:e] = rng.permutation(ci[s:e])
+        if e - s > 3:
+            ci[s + 1] = ci[s]
+    U = S.HostCSR(A.rows, A.cols, A.row_ptr.copy(), ci, A.values.copy())
+    B = K.dense(2000, 128, 6)
+    assert_parity(run(cuda, U, B, S.CSR_ROWWARP, tuning=S.CsrTuning(k_phases=4)), U, B, S.CSR_ROWWARP)
+
+
+def test_plan_with_column_phases(cuda):
+    torch = cuda
+    A, B = K.config("c1")
+    N = B.shape[1]
+    rp, ci, v = _dev(torch, A.row_ptr), _dev(torch, A.col_idx), _dev(torch, A.values)
+    view = S.device_view(A.rows, A.cols, rp, ci, v)
+    plan = S.CsrPlan(view, N, tuning=S.CsrTuning(k_phases=3), stream=torch.cuda.current_stream())
+    assert plan.algo == S.CSR_ROWWARP and plan.k_phases == 3
+    Bd = _dev(torch, B)
+    for _ in range(3):  # the plan keeps its split positions across executions
+        Cd = torch.full((A.rows, N), float("nan"), device="cuda")
+        plan.execute(Bd, Cd, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        assert_parity(Cd.cpu().numpy(), A, B, S.CSR_ROWWARP)
+    plan.close()
+    for bad in (-1, 9):
+        with pytest.raises(S.SpmmError) as e:
+            S.csr_workspace_size(view, N, S.CSR_ROWWARP, S.CsrTuning(k_phases=bad))
+        assert e.value.status == -1
+
+
 def test_config5_full_size_properties(cuda):
     """C5 at its full size (131072^2, ~17.2M nnz, N=256): exact rows on a sample, and a
     size-independent identity for the whole product, C @ x == A @ (B @ x)."""
