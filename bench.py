@@ -12,9 +12,15 @@ NCCL, and each rank computes its rows of C -- the total work is fixed ("strong" 
 One step = one SpMM of the rank's row range, inputs resident in HBM. `value` is whole-job
 GFLOP/s, 2*nnz*N / (max over ranks of the device time of the K timed steps / K). The inputs
 (406 MB at N=1) are larger than the 126 MB L2, so no flush is needed between steps.
-`e2e` repeats the measurement through the host-buffer C entry point (spmm_csr_f32_host):
-per step, host->device copies of the rank's A rows and of B from pinned memory, the kernel,
-and the device->host copy of the rank's C rows.
+`e2e` repeats the measurement from pinned host buffers. At one GPU through the host-buffer
+C entry point (spmm_csr_f32_host): per step, host->device copies of A and B, the kernel, and
+the device->host copy of C. At N GPUs as spmm_multigpu moves data: per step every rank copies
+its A rows in, rank 0 copies B in once and broadcasts it over NVLink (NCCL), every rank runs
+its plan and copies its C rows out.
+
+`roofline` carries the HBM fraction of the compulsory bytes (the reference's roofline model)
+and, for the CSR kernels, `gather_ceiling`: the rate at which the kernel pulls B rows into the
+SMs against a load-only probe of random 1 KB row fetches from an L2-resident part of B.
 
 `--impl reference` times the reference's CSR x dense semantics on the host cores (the
 oracle's OpenMP port: the reference ships no CPU SpMM of its own) on rank 0 only.
@@ -144,7 +150,7 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-# ------------------------------------------------------------------------ CPU baseline
+# ------------------------------------------------------------------------ gather ceiling
 
 
 def gather_ceiling(torch, Bd, rows: int, fetches: int, stream) -> float | None:
@@ -176,6 +182,9 @@ def gather_ceiling(torch, Bd, rows: int, fetches: int, stream) -> float | None:
         if i >= 2:
             ts.append(a.elapsed_time(b))
     return fetches * 1024.0 / (statistics.median(ts) * 1e-3) / 1e9
+
+
+# ------------------------------------------------------------------------ CPU baseline
 
 
 def cpu_baseline_run(A, B, steps: int, warmup: int):
@@ -434,16 +443,17 @@ def main():
         gathered = 4.0 * Ar.nnz * N  # B-row bytes the gather moves through L2 per launch
         gather_gbs = gathered / (avg_launch_ms * 1e-3) / 1e9
         roofline["l2_gather_gbs"] = round(gather_gbs, 1)
-        # The ceiling that actually bounds a uniform gather: whole random B rows pulled into
-        # the SMs, measured by a load-only probe over B's own footprint and over an L2-resident
-        # 32 MB part of it.
-        same = gather_ceiling(torch, Bd, A.cols, Ar.nnz, stream)
+        # The ceiling that bounds a gather of whole B rows: a load-only probe that pulls random
+        # 1 KB rows into the SMs from an L2-resident 32 MB part of B (the fastest any gather can
+        # go), and the same probe over B's whole footprint (uniformly random rows, so it misses
+        # L2 more often than the kernel, whose warps walk their sorted columns together).
         resident = gather_ceiling(torch, Bd, min(A.cols, 32768), Ar.nnz, stream)
-        if same:
+        same = gather_ceiling(torch, Bd, A.cols, Ar.nnz, stream)
+        if resident:
             roofline["gather_ceiling"] = {
-                "achieved_gbs": round(gather_gbs, 1), "ceiling_gbs": round(same, 1),
-                "frac": round(gather_gbs / same, 4), "l2_resident_ceiling_gbs": round(resident or 0.0, 1),
-                "probe": "random 1 KB B-row fetches over B's footprint, load-only (lib/libspmm_probe.so)"}
+                "achieved_gbs": round(gather_gbs, 1), "ceiling_gbs": round(resident, 1),
+                "frac": round(gather_gbs / resident, 4), "same_footprint_probe_gbs": round(same or 0.0, 1),
+                "probe": "load-only random 1 KB B-row fetches, L2-resident 32 MB (lib/libspmm_probe.so)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -41,15 +41,21 @@ __global__ void max_row_kernel(const int* __restrict__ row_ptr, int M, int* out)
     if ((threadIdx.x & 31) == 0) atomicMax(out, best);
 }
 
-// Column phases for ROWWARP: enough that each phase's share of B (K / phases rows of N
-// floats) fits in kPhaseL2Share of the L2.
-constexpr double kPhaseL2Share = 0.0;  // 0: phases off unless the caller asks
-
+// Column phases for ROWWARP. A random-row gather runs at the L2 rate (about 19-20 TB/s on
+// B200) while B fits in about 80 % of the L2, and falls towards the HBM rate beyond it
+// (14 TB/s at 128 MiB, 8 TB/s at 512 MiB). Phases of about half the L2 each bring B back
+// into range at the price of re-reading and re-writing C per phase and one launch per
+// phase, which only pays off on large launches. Measured on B200 (131072 rows x 131 nnz,
+// N = 256): 160 MiB of B 3 phases -4 %, 256 MiB 4 phases -13 %, 512 MiB 8 phases -38 %
+// of the time; at 128 MiB (config 5) 2 phases tie with one, and launches of 65536 or 16384
+// rows with 128 MiB of B got 3 % and 7 % slower. So: B above 1.2x the L2 and >= 12 GB gathered.
 int auto_phases(const spmm_csr_view* A, int32_t N, const DeviceState* st) {
-    if (kPhaseL2Share <= 0.0 || st->l2_bytes <= 0) return 1;
+    if (st->l2_bytes <= 0) return 1;
     const double b_bytes = 4.0 * A->cols * static_cast<double>(N);
-    const double share = kPhaseL2Share * st->l2_bytes;
-    int ph = static_cast<int>((b_bytes + share - 1) / share);
+    const double gather_bytes = 4.0 * A->nnz * static_cast<double>(N);
+    const double l2 = st->l2_bytes;
+    if (b_bytes <= 1.2 * l2 || gather_bytes < 12e9) return 1;
+    const int ph = static_cast<int>(b_bytes / (0.5 * l2) + 0.5);
     return std::min(std::max(ph, 1), 8);
 }
 

@@ -12,6 +12,14 @@ CSR/TC crossover in fill-in is what the hybrid threshold is set from.
     python sparse-matrix-multiplication_b200/sweep.py --out sweep.csv [--quick] [--n 256]
 
 Times are CUDA-event medians of single launches with a 256 MiB L2 flush in between.
+
+    python sparse-matrix-multiplication_b200/sweep.py --gather-footprints --out gather.csv
+
+instead measures the gather ceiling that bounds the FP32 CSR kernels: for B footprints from 8 MB
+to 512 MB (N = 256, so one B row is 1 KB) it times the load-only random-row probe
+(lib/libspmm_probe.so) and the planned CSR kernel on a 131072-row uniform matrix with 131
+nonzeros per row over that many columns (the fast generator), and reports both as GB/s of
+gathered B rows.
 """
 from __future__ import annotations
 
@@ -67,6 +75,79 @@ def time_ms(torch, fn, reps: int, flush) -> float:
     return float(np.median(ts))
 
 
+def gather_footprints(args) -> None:
+    import ctypes as C
+
+    import torch
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    probe = C.CDLL(str(HERE / "lib" / "libspmm_probe.so"))
+    probe.spmm_probe_gather.argtypes = [C.c_void_p, C.c_uint32, C.c_longlong, C.c_uint32, C.c_void_p, C.c_void_p]
+    ctas = C.c_int()
+    if probe.spmm_probe_ctas(C.byref(ctas)) != 0:
+        raise SystemExit("spmm_probe_ctas failed")
+    out = torch.empty(ctas.value * 256, dtype=torch.float32, device=dev)
+    M, N, per_row = 131072, 256, 131
+    fields = ["footprint_mb", "cols", "nnz", "probe_ms", "probe_gbs", "csr_ms", "csr_gbs", "csr_frac_of_probe",
+              "csr_gflops", "k_phases", "phased_k", "phased_ms"]
+    with open(args.out, "w", newline="") as fh:
+        w = csv.DictWriter(fh, fieldnames=fields)
+        w.writeheader()
+        for mb in (8, 16, 32, 48, 64, 80, 96, 112, 128, 160, 256, 512):
+            K = mb * 1024
+            A = S.generate_uniform_csr_fast(M, K, per_row / K, 42)
+            Bd = torch.empty((K, N), dtype=torch.float32, device=dev).uniform_(-1, 1)
+            rp, ci, v = (torch.from_numpy(x).to(dev) for x in (A.row_ptr, A.col_idx, A.values))
+            Cd = torch.empty((M, N), dtype=torch.float32, device=dev)
+            view = S.device_view(M, K, rp, ci, v)
+            plan = S.CsrPlan(view, N, stream=stream)
+
+            def run_probe(i=[0]):
+                i[0] += 1
+                rc = probe.spmm_probe_gather(C.c_void_p(Bd.data_ptr()), K, A.nnz - A.nnz % 4, i[0],
+                                             C.c_void_p(out.data_ptr()), C.c_void_p(stream.cuda_stream))
+                if rc:
+                    raise SystemExit(f"probe failed ({rc})")
+
+            def back_to_back(fn, reps=9):
+                fn()
+                torch.cuda.synchronize()
+                ts = []
+                for _ in range(reps):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    fn()
+                    b.record()
+                    torch.cuda.synchronize()
+                    ts.append(a.elapsed_time(b))
+                return float(np.median(ts))
+
+            pm = back_to_back(run_probe)
+            cm = back_to_back(lambda: plan.execute(Bd, Cd, stream))
+            ph, phm = 1, None
+            if mb > 96:  # column phases sized to ~64 MB of B each
+                ph = min(8, -(-mb // 64))
+                pplan = S.CsrPlan(view, N, tuning=S.CsrTuning(k_phases=ph), stream=stream)
+                phm = back_to_back(lambda: pplan.execute(Bd, Cd, stream))
+                pplan.close()
+            pg = (A.nnz - A.nnz % 4) * 1024 / (pm * 1e-3) / 1e9
+            cg = A.nnz * 1024 / (cm * 1e-3) / 1e9
+            row = {"footprint_mb": mb, "cols": K, "nnz": A.nnz, "probe_ms": round(pm, 4), "probe_gbs": round(pg, 1),
+                   "csr_ms": round(cm, 4), "csr_gbs": round(cg, 1), "csr_frac_of_probe": round(cg / pg, 4),
+                   "csr_gflops": round(2.0 * A.nnz * N / (cm * 1e-3) / 1e9, 1), "k_phases": plan.k_phases,
+                   "phased_k": ph, "phased_ms": round(phm, 4) if phm else ""}
+            w.writerow(row)
+            fh.flush()
+            print(json.dumps(row), flush=True)
+            plan.close()
+            del Bd, Cd, rp, ci, v
+    code, detail = S.device_error(0)
+    if code:
+        raise SystemExit(f"device error {code} ({detail})")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--out", type=Path, required=True)
@@ -74,7 +155,12 @@ def main():
     ap.add_argument("--reps", type=int, default=15)
     ap.add_argument("--threshold", type=float, default=0.0, help="hybrid fill-in threshold (0 = library default)")
     ap.add_argument("--quick", action="store_true")
+    ap.add_argument("--gather-footprints", action="store_true",
+                    help="probe vs CSR kernel gather rate over B footprints (see above)")
     args = ap.parse_args()
+    if args.gather_footprints:
+        gather_footprints(args)
+        return
 
     import torch
 
