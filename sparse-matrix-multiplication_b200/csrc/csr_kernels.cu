@@ -150,11 +150,38 @@ __device__ __forceinline__ int lane_col(int col0, int r, int lane) {
 
 __device__ __forceinline__ int clampi(int x, int lo, int hi) { return x < lo ? lo : (x > hi ? hi : x); }
 
+// Per-warp staging ring for A's (col, val) pairs: two groups of 32, filled with cp.async
+// (global -> shared, no registers held while in flight) one group ahead of use, read back
+// as one broadcast 8-byte shared load per nonzero.
+struct PairRing {
+    int2 g[2][32];
+};
+
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int Pending>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(Pending) : "memory");
+}
+
+// Copy the pairs [base, min(base + 32, p1)) of A into ring slot `slot` (one commit group).
+__device__ __forceinline__ void stage_pairs(const CsrArgs& a, PairRing* ring, int slot, int base, int p1, int lane) {
+    const int p = base + lane;
+    if (p < p1) {
+        cp_async4(&ring->g[slot][lane].x, a.col_idx + p);
+        cp_async4(&ring->g[slot][lane].y, a.values + p);
+    }
+    cp_async_commit();
+}
+
 // Sum of v_p * B[col_p, slab columns] over p in [p0, p1) into acc (caller zeroes acc), as
 // one sequential FMA chain per column.
 template <int VEC, int R, int U>
-__device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int col0, int lane, uint64_t pol,
-                                           float (&acc)[R][VEC]) {
+__device__ __forceinline__ void accumulate(const CsrArgs& a, PairRing* ring, int p0, int p1, int col0, int lane,
+                                           uint64_t pol, float (&acc)[R][VEC]) {
     using V = Vec<VEC>;
     const int hint = a.b_policy;
     bool ok[R];
@@ -162,35 +189,33 @@ __device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int
     for (int r = 0; r < R; ++r) ok[r] = lane_col<VEC>(col0, r, lane) < a.N;
 
     const float* __restrict__ Bp = a.B + col0 + lane * VEC;
-    int base = p0;
-    int kk = 0;
-    float vv = 0.f;
-    if (base < p1 && lane < p1 - base) {
-        kk = __ldcs(a.col_idx + base + lane);
-        vv = __ldcs(a.values + base + lane);
-    }
-    while (base < p1) {
+    if (p0 >= p1) return;
+    stage_pairs(a, ring, 0, p0, p1, lane);
+    int slot = 0;
+    for (int base = p0; base < p1; base += 32) {
+        stage_pairs(a, ring, slot ^ 1, base + 32, p1, lane);  // next group (empty past p1)
+        cp_async_wait<1>();
+        __syncwarp();
         const int cnt = min(32, p1 - base);
-        // Prefetch the next group of (col, val) pairs.
-        const int nbase = base + 32;
-        int nk = 0;
-        float nv = 0.f;
-        if (nbase < p1 && lane < p1 - nbase) {
-            nk = __ldcs(a.col_idx + nbase + lane);
-            nv = __ldcs(a.values + nbase + lane);
-        }
-        if (lane < cnt && static_cast<unsigned>(kk) >= static_cast<unsigned>(a.K)) {
+        if (lane < cnt && static_cast<unsigned>(ring->g[slot][lane].x) >= static_cast<unsigned>(a.K)) {
             record_device_error(a.err, SPMM_ERR_BAD_INDEX, static_cast<long long>(base + lane));
-            kk = 0;
-            vv = 0.f;
+            ring->g[slot][lane] = make_int2(0, 0);
         }
+        __syncwarp();
+        const int2* grp = ring->g[slot];
         int q = 0;
         for (; q + U <= cnt; q += U) {
+            // Two strides per nonzero (R = 2): keep the U values from the 8-byte pair loads;
+            // one stride: re-read each value at its FMA (fewer live registers; measured
+            // faster on configs 1, 2 and 4, slower on config 5).
+            constexpr bool kKeepV = R >= 2;
             typename V::T b[U][R];
+            float v[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int k = __shfl_sync(kFull, kk, q + u);
-                const float* brow = Bp + static_cast<size_t>(k) * a.N;
+                const int2 pr = grp[q + u];
+                if constexpr (kKeepV) v[u] = __int_as_float(pr.y);
+                const float* brow = Bp + static_cast<size_t>(pr.x) * a.N;
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
                     if (ok[r]) b[u][r] = V::load(brow + r * 32 * VEC, pol, hint);
@@ -199,17 +224,17 @@ __device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const float v = __shfl_sync(kFull, vv, q + u);
+                const float vu = kKeepV ? v[u] : __int_as_float(grp[q + u].y);
 #pragma unroll
                 for (int r = 0; r < R; ++r)
 #pragma unroll
-                    for (int e = 0; e < VEC; ++e) acc[r][e] = fmaf(v, V::get(b[u][r], e), acc[r][e]);
+                    for (int e = 0; e < VEC; ++e) acc[r][e] = fmaf(vu, V::get(b[u][r], e), acc[r][e]);
             }
         }
         for (; q < cnt; ++q) {
-            const int k = __shfl_sync(kFull, kk, q);
-            const float v = __shfl_sync(kFull, vv, q);
-            const float* brow = Bp + static_cast<size_t>(k) * a.N;
+            const int2 pr = grp[q];
+            const float v = __int_as_float(pr.y);
+            const float* brow = Bp + static_cast<size_t>(pr.x) * a.N;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 if (ok[r]) {
@@ -219,10 +244,10 @@ __device__ __forceinline__ void accumulate(const CsrArgs& a, int p0, int p1, int
                 }
             }
         }
-        base = nbase;
-        kk = nk;
-        vv = nv;
+        __syncwarp();  // every lane is done with this slot before it is refilled
+        slot ^= 1;
     }
+    cp_async_wait<0>();
 }
 
 template <int VEC, int R>
@@ -277,6 +302,8 @@ __device__ __forceinline__ void row_bounds(const CsrArgs& a, int i, int& rs, int
 template <int VEC, int R, int U, bool PHASED>
 __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kernel(CsrArgs a) {
     constexpr int W = 32 * VEC * R;
+    __shared__ PairRing rings[kWarpsPerCta];
+    PairRing* ring = &rings[threadIdx.x >> 5];
     const int lane = threadIdx.x & 31;
     const int warp = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
     const int nwarps = gridDim.x * kWarpsPerCta;
@@ -296,10 +323,10 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kerne
             if (a.phase > 0 && lo == hi) continue;
             if (a.phase > 0) load_slab<VEC, R>(a, crow, col0, lane, acc);
             else zero(acc);
-            accumulate<VEC, R, U>(a, lo, hi, col0, lane, pol, acc);
+            accumulate<VEC, R, U>(a, ring, lo, hi, col0, lane, pol, acc);
         } else {
             zero(acc);
-            accumulate<VEC, R, U>(a, rs, re, col0, lane, pol, acc);
+            accumulate<VEC, R, U>(a, ring, rs, re, col0, lane, pol, acc);
         }
         store_slab<VEC, R>(a, crow, col0, lane, acc, true);
     }
@@ -371,12 +398,12 @@ __device__ __forceinline__ int warp_forward_bound(const CsrArgs& a, int r0, long
 // One piece [p0, p1) of long row i (rs..re) for this CTA's slab; `slot` is this chunk's
 // workspace slot.
 template <int VEC, int R, int U>
-__device__ __forceinline__ void long_piece(const CsrArgs& a, int i, int rs, int re, int p0, int p1, int slot,
-                                           int col0, int lane, uint64_t pol) {
+__device__ __forceinline__ void long_piece(const CsrArgs& a, PairRing* ring, int i, int rs, int re, int p0, int p1,
+                                           int slot, int col0, int lane, uint64_t pol) {
     using V = Vec<VEC>;
     float acc[R][VEC];
     zero(acc);
-    accumulate<VEC, R, U>(a, p0, p1, col0, lane, pol, acc);
+    accumulate<VEC, R, U>(a, ring, p0, p1, col0, lane, pol, acc);
     store_slab<VEC, R>(a, a.partials + static_cast<size_t>(slot) * a.N, col0, lane, acc, false);
     // Publish the piece, then count arrivals on the row's first chunk (per slab).
     __threadfence();
@@ -419,6 +446,8 @@ __device__ __forceinline__ void long_piece(const CsrArgs& a, int i, int rs, int 
 template <int VEC, int R, int U>
 __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(CsrArgs a) {
     constexpr int W = 32 * VEC * R;
+    __shared__ PairRing rings[kWarpsPerCta];
+    PairRing* ring = &rings[threadIdx.x >> 5];
     const int lane = threadIdx.x & 31;
     const int c = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
     if (c >= a.num_chunks) return;
@@ -437,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(
         if (qe - qs > a.S) {
             const int p0 = static_cast<int>(max(static_cast<long long>(qs), d0 - q));
             const int p1 = static_cast<int>(min(static_cast<long long>(qe), d1 - q));
-            if (p0 < p1) long_piece<VEC, R, U>(a, q, qs, qe, p0, p1, 2 * c, col0, lane, pol);
+            if (p0 < p1) long_piece<VEC, R, U>(a, ring, q, qs, qe, p0, p1, 2 * c, col0, lane, pol);
         }
     }
     // Rows whose first item lies in this chunk.
@@ -447,11 +476,11 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(
         if (re - rs <= a.S) {
             float acc[R][VEC];
             zero(acc);
-            accumulate<VEC, R, U>(a, rs, re, col0, lane, pol, acc);
+            accumulate<VEC, R, U>(a, ring, rs, re, col0, lane, pol, acc);
             store_slab<VEC, R>(a, a.C + static_cast<size_t>(i) * a.N, col0, lane, acc, true);
         } else {
             const int p1 = static_cast<int>(min(static_cast<long long>(re), d1 - i));
-            long_piece<VEC, R, U>(a, i, rs, re, rs, max(p1, rs), 2 * c + 1, col0, lane, pol);
+            long_piece<VEC, R, U>(a, ring, i, rs, re, rs, max(p1, rs), 2 * c + 1, col0, lane, pol);
         }
     }
 }
