@@ -179,11 +179,17 @@ __device__ __forceinline__ void stage_pairs(const CsrArgs& a, PairRing* ring, in
 
 // Sum of v_p * B[col_p, slab columns] over p in [p0, p1) into acc (caller zeroes acc), as
 // one sequential FMA chain per column.
-template <int VEC, int R, int U>
+template <int VEC, int R, int U, bool HINT>
 __device__ __forceinline__ void accumulate(const CsrArgs& a, PairRing* ring, int p0, int p1, int col0, int lane,
                                            uint64_t pol, float (&acc)[R][VEC]) {
     using V = Vec<VEC>;
     const int hint = a.b_policy;
+    // B row loads: plain non-coherent loads unless the caller asked for an L2 policy (a
+    // separate instantiation, so the default kernels carry no policy register or branch).
+    auto load_b = [&](const float* p) {
+        if constexpr (HINT) return V::load(p, pol, hint);
+        else return V::load(p, 0, 0);
+    };
     bool ok[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) ok[r] = lane_col<VEC>(col0, r, lane) < a.N;
@@ -218,7 +224,7 @@ __device__ __forceinline__ void accumulate(const CsrArgs& a, PairRing* ring, int
                 const float* brow = Bp + static_cast<size_t>(pr.x) * a.N;
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
-                    if (ok[r]) b[u][r] = V::load(brow + r * 32 * VEC, pol, hint);
+                    if (ok[r]) b[u][r] = load_b(brow + r * 32 * VEC);
                     else b[u][r] = typename V::T{};
                 }
             }
@@ -238,7 +244,7 @@ __device__ __forceinline__ void accumulate(const CsrArgs& a, PairRing* ring, int
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 if (ok[r]) {
-                    const typename V::T b = V::load(brow + r * 32 * VEC, pol, hint);
+                    const typename V::T b = load_b(brow + r * 32 * VEC);
 #pragma unroll
                     for (int e = 0; e < VEC; ++e) acc[r][e] = fmaf(v, V::get(b, e), acc[r][e]);
                 }
@@ -299,7 +305,7 @@ __device__ __forceinline__ void row_bounds(const CsrArgs& a, int i, int& rs, int
         record_device_error(a.err, SPMM_ERR_BAD_INDEX, -1 - static_cast<long long>(i));
 }
 
-template <int VEC, int R, int U, bool PHASED>
+template <int VEC, int R, int U, bool PHASED, bool HINT>
 __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kernel(CsrArgs a) {
     constexpr int W = 32 * VEC * R;
     __shared__ PairRing rings[kWarpsPerCta];
@@ -308,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kerne
     const int warp = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
     const int nwarps = gridDim.x * kWarpsPerCta;
     const int col0 = blockIdx.y * W;
-    const uint64_t pol = evict_last_policy();
+    const uint64_t pol = HINT ? evict_last_policy() : 0;
     for (int i = warp; i < a.M; i += nwarps) {
         int rs, re;
         row_bounds(a, i, rs, re);
@@ -323,10 +329,10 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kerne
             if (a.phase > 0 && lo == hi) continue;
             if (a.phase > 0) load_slab<VEC, R>(a, crow, col0, lane, acc);
             else zero(acc);
-            accumulate<VEC, R, U>(a, ring, lo, hi, col0, lane, pol, acc);
+            accumulate<VEC, R, U, HINT>(a, ring, lo, hi, col0, lane, pol, acc);
         } else {
             zero(acc);
-            accumulate<VEC, R, U>(a, ring, rs, re, col0, lane, pol, acc);
+            accumulate<VEC, R, U, HINT>(a, ring, rs, re, col0, lane, pol, acc);
         }
         store_slab<VEC, R>(a, crow, col0, lane, acc, true);
     }
@@ -397,13 +403,13 @@ __device__ __forceinline__ int warp_forward_bound(const CsrArgs& a, int r0, long
 
 // One piece [p0, p1) of long row i (rs..re) for this CTA's slab; `slot` is this chunk's
 // workspace slot.
-template <int VEC, int R, int U>
+template <int VEC, int R, int U, bool HINT>
 __device__ __forceinline__ void long_piece(const CsrArgs& a, PairRing* ring, int i, int rs, int re, int p0, int p1,
                                            int slot, int col0, int lane, uint64_t pol) {
     using V = Vec<VEC>;
     float acc[R][VEC];
     zero(acc);
-    accumulate<VEC, R, U>(a, ring, p0, p1, col0, lane, pol, acc);
+    accumulate<VEC, R, U, HINT>(a, ring, p0, p1, col0, lane, pol, acc);
     store_slab<VEC, R>(a, a.partials + static_cast<size_t>(slot) * a.N, col0, lane, acc, false);
     // Publish the piece, then count arrivals on the row's first chunk (per slab).
     __threadfence();
@@ -443,7 +449,7 @@ __device__ __forceinline__ void long_piece(const CsrArgs& a, PairRing* ring, int
     if (lane == 0) *counter = 0;
 }
 
-template <int VEC, int R, int U>
+template <int VEC, int R, int U, bool HINT>
 __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(CsrArgs a) {
     constexpr int W = 32 * VEC * R;
     __shared__ PairRing rings[kWarpsPerCta];
@@ -452,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(
     const int c = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
     if (c >= a.num_chunks) return;
     const int col0 = blockIdx.y * W;
-    const uint64_t pol = evict_last_policy();
+    const uint64_t pol = HINT ? evict_last_policy() : 0;
     const long long d0 = static_cast<long long>(c) * a.S;
     const long long d1 = min(d0 + a.S, a.items);
     const int r0 = warp_lower_bound(a, d0, lane);
@@ -466,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(
         if (qe - qs > a.S) {
             const int p0 = static_cast<int>(max(static_cast<long long>(qs), d0 - q));
             const int p1 = static_cast<int>(min(static_cast<long long>(qe), d1 - q));
-            if (p0 < p1) long_piece<VEC, R, U>(a, ring, q, qs, qe, p0, p1, 2 * c, col0, lane, pol);
+            if (p0 < p1) long_piece<VEC, R, U, HINT>(a, ring, q, qs, qe, p0, p1, 2 * c, col0, lane, pol);
         }
     }
     // Rows whose first item lies in this chunk.
@@ -476,11 +482,11 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(
         if (re - rs <= a.S) {
             float acc[R][VEC];
             zero(acc);
-            accumulate<VEC, R, U>(a, ring, rs, re, col0, lane, pol, acc);
+            accumulate<VEC, R, U, HINT>(a, ring, rs, re, col0, lane, pol, acc);
             store_slab<VEC, R>(a, a.C + static_cast<size_t>(i) * a.N, col0, lane, acc, true);
         } else {
             const int p1 = static_cast<int>(min(static_cast<long long>(re), d1 - i));
-            long_piece<VEC, R, U>(a, ring, i, rs, re, rs, max(p1, rs), 2 * c + 1, col0, lane, pol);
+            long_piece<VEC, R, U, HINT>(a, ring, i, rs, re, rs, max(p1, rs), 2 * c + 1, col0, lane, pol);
         }
     }
 }
@@ -596,11 +602,18 @@ template <int VEC, int R>
 void launch_vr(int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
     // Eight vector loads per lane in flight: U nonzeros x R strides.
     constexpr int U = (8 / R) > 0 ? (8 / R) : 1;
+    const bool hint = a.b_policy != 0;
     if (algo == SPMM_CSR_ROWWARP) {
-        if (a.phases > 1) csr_rowwarp_kernel<VEC, R, U, true><<<grid, kThreads, 0, s>>>(a);
-        else csr_rowwarp_kernel<VEC, R, U, false><<<grid, kThreads, 0, s>>>(a);
+        if (a.phases > 1) {
+            if (hint) csr_rowwarp_kernel<VEC, R, U, true, true><<<grid, kThreads, 0, s>>>(a);
+            else csr_rowwarp_kernel<VEC, R, U, true, false><<<grid, kThreads, 0, s>>>(a);
+        } else {
+            if (hint) csr_rowwarp_kernel<VEC, R, U, false, true><<<grid, kThreads, 0, s>>>(a);
+            else csr_rowwarp_kernel<VEC, R, U, false, false><<<grid, kThreads, 0, s>>>(a);
+        }
     } else {
-        csr_merge_kernel<VEC, R, U><<<grid, kThreads, 0, s>>>(a);
+        if (hint) csr_merge_kernel<VEC, R, U, true><<<grid, kThreads, 0, s>>>(a);
+        else csr_merge_kernel<VEC, R, U, false><<<grid, kThreads, 0, s>>>(a);
     }
 }
 

@@ -202,6 +202,18 @@ def test_plan_picks_distribution_and_matches(cuda, name, expect_algo):
     plan.close()
 
 
+@pytest.mark.parametrize("policy", [1, 2])
+@pytest.mark.parametrize("algo", [S.CSR_MERGE, S.CSR_ROWWARP])
+def test_b_load_policies_bit_exact(cuda, policy, algo):
+    # The L2 evict-last B loads are separate kernel instantiations; same arithmetic.
+    lens = np.random.default_rng(policy).integers(0, 120, size=600)
+    lens[5] = 2500
+    A = K.random_csr(600, 5000, lens, seed=policy + 10)
+    B = K.dense(5000, 192, 3)
+    t = S.CsrTuning(b_policy=policy)
+    assert_parity(run(cuda, A, B, algo, tuning=t), A, B, algo, tuning=t)
+
+
 @pytest.mark.parametrize("phases", [2, 3, 5, 8])
 @pytest.mark.parametrize("N", [64, 100, 257])
 def test_column_phases_bit_exact(cuda, phases, N):
