@@ -44,6 +44,14 @@
 #ifndef SPMM_CSR_MIN_CTAS
 #define SPMM_CSR_MIN_CTAS 4
 #endif
+// Nonzeros whose B loads are issued before their FMAs, for one and two 32-lane strides per
+// nonzero (compile-time tuning).
+#ifndef SPMM_CSR_UNROLL_R1
+#define SPMM_CSR_UNROLL_R1 8
+#endif
+#ifndef SPMM_CSR_UNROLL_R2
+#define SPMM_CSR_UNROLL_R2 4
+#endif
 
 namespace spmm_b200 {
 namespace {
@@ -600,8 +608,8 @@ size_t merge_workspace_bytes(long long num_chunks, int N) {
 
 template <int VEC, int R>
 void launch_vr(int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
-    // Eight vector loads per lane in flight: U nonzeros x R strides.
-    constexpr int U = (8 / R) > 0 ? (8 / R) : 1;
+    // Vector loads per lane in flight: U nonzeros x R strides (eight by default).
+    constexpr int U = R == 1 ? SPMM_CSR_UNROLL_R1 : (R == 2 ? SPMM_CSR_UNROLL_R2 : ((8 / R) > 0 ? (8 / R) : 1));
     const bool hint = a.b_policy != 0;
     if (algo == SPMM_CSR_ROWWARP) {
         if (a.phases > 1) {
