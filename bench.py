@@ -14,9 +14,9 @@ GFLOP/s, 2*nnz*N / (max over ranks of the device time of the K timed steps / K).
 (406 MB at N=1) are larger than the 126 MB L2, so no flush is needed between steps.
 `e2e` repeats the measurement from pinned host buffers. At one GPU through the host-buffer
 C entry point (spmm_csr_f32_host): per step, host->device copies of A and B, the kernel, and
-the device->host copy of C. At N GPUs as spmm_multigpu moves data: per step every rank copies
-its A rows in, rank 0 copies B in once and broadcasts it over NVLink (NCCL), every rank runs
-its plan and copies its C rows out.
+the device->host copy of C. At N GPUs: per step every rank copies its A rows in, B crosses the
+host links once in total (each rank copies 1/N of its rows, then an NCCL all-gather over
+NVLink), every rank runs its plan and copies its C rows out.
 
 `roofline` carries the HBM fraction of the compulsory bytes (the reference's roofline model)
 and, for the CSR kernels, `gather_ceiling`: the rate at which the kernel pulls B rows into the
@@ -363,21 +363,33 @@ def main():
     # ---- end to end through the host-buffer entry point
     e2e = None
     if not args.no_e2e and cfg_name != "c3" and world > 1:
-        # Multi-GPU end to end, the spmm_multigpu data flow: every rank copies its A rows
-        # host -> device, rank 0 copies B once and broadcasts it over NVLink (NCCL), every
-        # rank runs its plan (spmm_csr_plan_execute) and copies its C rows back.
+        # Multi-GPU end to end: every rank copies its A rows host -> device; B crosses the
+        # host links once in total -- each rank copies 1/N of B's rows and NCCL all-gathers
+        # them over NVLink (when N divides B's rows; else rank 0 copies B and broadcasts it,
+        # as spmm_multigpu does); every rank runs its plan (spmm_csr_plan_execute) and copies
+        # its C rows back.
         pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
         h_rp, h_ci, h_va = pin(Ar.row_ptr), pin(Ar.col_idx), pin(Ar.values)
-        h_b = pin(Bh) if rank == 0 else None
+        gather_b = A.cols % world == 0
+        if gather_b:
+            kb = A.cols // world
+            h_b = pin(np.ascontiguousarray(Bh[rank * kb:(rank + 1) * kb]))
+            b_part = Bd[rank * kb:(rank + 1) * kb]
+        else:
+            h_b = pin(Bh) if rank == 0 else None
         h_c = torch.empty((max(rows_r, 1), N), dtype=torch.float32).pin_memory()
 
         def e2e_step():
             rp.copy_(h_rp, non_blocking=True)
             ci.copy_(h_ci, non_blocking=True)
             va.copy_(h_va, non_blocking=True)
-            if rank == 0:
-                Bd.copy_(h_b, non_blocking=True)
-            dist.broadcast(Bd, src=0)
+            if gather_b:
+                b_part.copy_(h_b, non_blocking=True)
+                dist.all_gather_into_tensor(Bd, b_part)
+            else:
+                if rank == 0:
+                    Bd.copy_(h_b, non_blocking=True)
+                dist.broadcast(Bd, src=0)
             plan.execute(Bd, Cd, stream)
             h_c.copy_(Cd, non_blocking=True)
             torch.cuda.synchronize()
@@ -394,9 +406,10 @@ def main():
         e2e_ms = max_over_ranks(e2e_ms)
         h2d = sum_over_ranks(float(Ar.row_ptr.nbytes + Ar.col_idx.nbytes + Ar.values.nbytes)) + Bh.nbytes
         d2h = sum_over_ranks(float(rows_r * N * 4))
+        how = "1/N of B's rows H2D + NCCL all-gather" if gather_b else "B H2D on rank 0 + NCCL broadcast"
         e2e = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "api": "per rank: A rows H2D, B H2D on rank 0 + NCCL broadcast, spmm_csr_plan_execute, C rows D2H"}
+               "api": f"per rank: A rows H2D, {how}, spmm_csr_plan_execute, C rows D2H"}
     elif not args.no_e2e and cfg_name != "c3":
         pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
         hA = S.HostCSR(Ar.rows, Ar.cols, pin(Ar.row_ptr).numpy(), pin(Ar.col_idx).numpy(), pin(Ar.values).numpy())
