@@ -325,6 +325,19 @@ int spmm_multigpu_run(const spmm_csr_view* hA, const float* hB, float* hC, int32
 int spmm_unified_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
                      int32_t warmup, int32_t iters, float* ms);
 
+/* spmm_unified_run for matrices larger than the device (no counterpart in the reference, whose
+ * unified path prefetches everything and leaves the rest to demand paging). device_budget =
+ * bytes of device memory to plan with (0 = 90 % of what is free now). When B does not fit
+ * beside A, C and the split positions, A's columns are cut into phases (at most 32; *phases_used
+ * reports the count, 1 = no phases): per phase, B's rows of that column range are prefetched to
+ * the device, the phase's kernel continues every C element's FMA chain, and the rows are
+ * prefetched back to the host before the next phase. Results equal the one-warp-per-row kernel
+ * (the reference's sequential chain per element) bit for bit; *ms is the median time of a whole
+ * pass, migrations included. */
+int spmm_unified_run_ex(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
+                        size_t device_budget, int32_t warmup, int32_t iters, float* ms,
+                        int32_t* phases_used);
+
 #ifdef __cplusplus
 }
 #endif

@@ -81,5 +81,7 @@ int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, con
 size_t csr_f32_counter_bytes(const spmm_csr_view* A, int32_t N, const spmm_csr_tuning* tune, int sm_count);
 int csr_f32_chunk(const spmm_csr_view* A, const spmm_csr_tuning* tune, int sm_count);
 int csr_f32_ksplit(const spmm_csr_view* A, int phases, int* split, cudaStream_t stream, DeviceState* st);
+int csr_f32_phase_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int phases, int phase,
+                         int* split, cudaStream_t stream, DeviceState* st);
 
 }  // namespace spmm_b200

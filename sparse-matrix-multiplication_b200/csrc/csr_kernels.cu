@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kThreads) csr_ksplit_kernel(CsrArgs a) {
     const int lane = threadIdx.x & 31;
     const int warp = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
     const int nwarps = gridDim.x * kWarpsPerCta;
-    const int nb = a.phases - 1;  // <= 7
+    const int nb = a.phases - 1;  // <= 32: lane b keeps boundary b's count
     for (int i = warp; i < a.M; i += nwarps) {
         int rs, re;
         row_bounds(a, i, rs, re);
@@ -725,9 +725,11 @@ int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, con
     return SPMM_OK;
 }
 
-// Split positions for a plan that keeps them across executions.
+// Split positions for a plan that keeps them across executions (phases <= 33: one warp
+// lane per boundary).
 int csr_f32_ksplit(const spmm_csr_view* A, int phases, int* split, cudaStream_t stream, DeviceState* st) {
     if (phases <= 1 || A->rows == 0) return SPMM_OK;
+    if (phases > 33) return SPMM_ERR_INVALID_ARG;
     CsrArgs a{};
     a.M = A->rows;
     a.K = A->cols;
@@ -739,6 +741,38 @@ int csr_f32_ksplit(const spmm_csr_view* A, int phases, int* split, cudaStream_t 
     a.err = st->err;
     const long long warps = std::min<long long>(A->rows, static_cast<long long>(st->sm_count) * 64);
     csr_ksplit_kernel<<<static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta), kThreads, 0, stream>>>(a);
+    SPMM_CUDA_TRY(cudaGetLastError());
+    return SPMM_OK;
+}
+
+// One column phase of the ROWWARP kernel (callers that interleave other work between
+// phases, e.g. moving B's slices in and out of device memory); `split` holds the
+// (phases - 1) x M positions from csr_f32_ksplit.
+int csr_f32_phase_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int phases, int phase,
+                         int* split, cudaStream_t stream, DeviceState* st) {
+    SPMM_TRY(check_view(A, B, C, N));
+    if (phases < 1 || phase < 0 || phase >= phases || (phases > 1 && !split)) return SPMM_ERR_INVALID_ARG;
+    if (A->rows == 0 || N == 0) return SPMM_OK;
+    CsrArgs a{};
+    a.M = A->rows;
+    a.K = A->cols;
+    a.N = N;
+    a.nnz = A->nnz;
+    a.row_ptr = A->row_ptr;
+    a.col_idx = A->col_idx;
+    a.values = A->values;
+    a.B = B;
+    a.C = C;
+    a.err = st->err;
+    a.phases = phases;
+    a.phase = phase;
+    a.ksplit = split;
+    const Geometry g = pick_geometry(B, C, N, slab_width(N, 0));
+    const int slabs = (N + g.width() - 1) / g.width();
+    if (slabs > 65535) return SPMM_ERR_TOO_LARGE;
+    const long long warps = std::min<long long>(A->rows, static_cast<long long>(st->sm_count) * 64);
+    const dim3 grid(static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta), slabs, 1);
+    launch(g, SPMM_CSR_ROWWARP, a, grid, stream);
     SPMM_CUDA_TRY(cudaGetLastError());
     return SPMM_OK;
 }

@@ -472,10 +472,33 @@ int spmm_multigpu_run(const spmm_csr_view* hA, const float* hB, float* hC, int32
 
 int spmm_unified_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, int32_t warmup, int32_t iters,
                      float* ms) {
+    return spmm_unified_run_ex(hA, hB, hC, N, 0, warmup, iters, ms, nullptr);
+}
+
+int spmm_unified_run_ex(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, size_t device_budget,
+                        int32_t warmup, int32_t iters, float* ms, int32_t* phases_used) {
     if (!check_host_view(hA) || N < 0 || warmup < 0 || iters < 1 || !ms) return SPMM_ERR_INVALID_ARG;
     DeviceState* st = nullptr;
     SPMM_TRY(current_device_state(&st));
     const size_t M = hA->rows, K = hA->cols, nnz = hA->nnz;
+    // Device bytes for everything but B (A, C, split positions) and for B.
+    const size_t b_bytes = sizeof(float) * K * N;
+    const size_t rest_bytes = sizeof(int) * (M + 1) + 8 * nnz + sizeof(float) * M * N + sizeof(int) * 32 * M + (64u << 20);
+    if (device_budget == 0) {
+        size_t free_b = 0, total_b = 0;
+        SPMM_CUDA_TRY(cudaMemGetInfo(&free_b, &total_b));
+        device_budget = free_b / 10 * 9;
+    }
+    // B in column phases when it does not fit beside the rest: each phase's rows of B are
+    // moved to the device, used, and moved back before the next (at most 32 phases; beyond
+    // that, or when even A and C do not fit, the driver pages on demand).
+    int phases = 1;
+    if (b_bytes + rest_bytes > device_budget && rest_bytes < device_budget && K > 1 && N > 0) {
+        const size_t per = device_budget - rest_bytes;
+        const size_t want = (b_bytes + per - 1) / per;
+        if (want <= 32) phases = static_cast<int>(std::max<size_t>(want, 2));
+    }
+    if (phases_used) *phases_used = phases;
     int* rp = nullptr;
     int* ci = nullptr;
     float* v = nullptr;
@@ -507,13 +530,39 @@ int spmm_unified_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_
         cudaMemPrefetchAsync(rp, sizeof(int) * (M + 1), st->device, s);
         cudaMemPrefetchAsync(ci, sizeof(int) * std::max<size_t>(nnz, 1), st->device, s);
         cudaMemPrefetchAsync(v, sizeof(float) * std::max<size_t>(nnz, 1), st->device, s);
-        cudaMemPrefetchAsync(B, sizeof(float) * std::max<size_t>(K * N, 1), st->device, s);
+        if (phases == 1) cudaMemPrefetchAsync(B, sizeof(float) * std::max<size_t>(K * N, 1), st->device, s);
         cudaMemPrefetchAsync(C, sizeof(float) * std::max<size_t>(M * N, 1), st->device, s);
         cudaGetLastError();
         spmm_csr_view d = *hA;
         d.row_ptr = rp;
         d.col_idx = ci;
         d.values = v;
+        if (phases > 1) {
+            // Column phases: split positions once, then per pass and phase p: B rows
+            // [K p / P, K (p + 1) / P) to the device, the phase's launch, the rows back.
+            if (cudaMalloc(&ws, sizeof(int) * (phases - 1) * std::max<size_t>(M, 1)) != cudaSuccess) {
+                rc = SPMM_ERR_NO_MEMORY;
+                break;
+            }
+            rc = csr_f32_ksplit(&d, phases, static_cast<int*>(ws), s, st);
+            if (rc != SPMM_OK) break;
+            auto pass = [&]() -> int {
+                for (int p = 0; p < phases; ++p) {
+                    const size_t k0 = K * p / phases, k1 = K * (p + 1) / phases;
+                    float* slice = B + k0 * N;
+                    const size_t bytes = sizeof(float) * (k1 - k0) * N;
+                    if (bytes) cudaMemPrefetchAsync(slice, bytes, st->device, s);
+                    SPMM_TRY(csr_f32_phase_launch(&d, B, C, N, phases, p, static_cast<int*>(ws), s, st));
+                    if (bytes) cudaMemPrefetchAsync(slice, bytes, cudaCpuDeviceId, s);
+                }
+                cudaGetLastError();
+                return SPMM_OK;
+            };
+            rc = time_launches(pass, warmup, iters, s, ms);
+            if (rc == SPMM_OK && cudaStreamSynchronize(s) != cudaSuccess) rc = SPMM_ERR_CUDA;
+            if (rc == SPMM_OK && M * N != 0) std::memcpy(hC, C, sizeof(float) * M * N);
+            break;
+        }
         size_t need = 0;
         rc = csr_f32_workspace_bytes(&d, N, SPMM_CSR_AUTO, nullptr, st->sm_count, &need);
         if (rc != SPMM_OK) break;

@@ -36,6 +36,7 @@ EXPORTS = [
     "spmm_csr_f32_ws", "spmm_csr_f32_chunk", "spmm_csr_f32_host", "spmm_convert_f32", "spmm_bsr16",
     "spmm_bsr16_algo", "spmm_device_error", "spmm_hybrid_default_threshold", "spmm_hybrid_choose",
     "spmm_backend_name", "spmm_hybrid_run", "spmm_gpu_count", "spmm_multigpu_run", "spmm_unified_run",
+    "spmm_unified_run_ex",
     "spmm_csr_f32_noalloc", "spmm_csr_to_bsr16_device_count", "spmm_csr_to_bsr16_device_fill",
     "spmm_csr_plan_create", "spmm_csr_plan_execute", "spmm_csr_plan_info", "spmm_csr_plan_destroy",
     "spmm_csr_plan_k_phases",
@@ -135,6 +136,8 @@ def lib() -> C.CDLL:
         "spmm_multigpu_run": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, i32, i32, C.POINTER(f32),
                                         C.POINTER(i32), vp, vp, C.POINTER(f32)]),
         "spmm_unified_run": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, i32, C.POINTER(f32)]),
+        "spmm_unified_run_ex": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, C.c_size_t, i32, i32, C.POINTER(f32),
+                                          C.POINTER(i32)]),
         "spmm_csr_f32_noalloc": (C.c_int, [C.POINTER(CsrView), vp, vp, i32, i32, vp]),
         "spmm_csr_to_bsr16_device_count": (C.c_int, [C.POINTER(CsrView), vp, C.POINTER(i32), vp]),
         "spmm_csr_to_bsr16_device_fill": (C.c_int, [C.POINTER(CsrView), vp, vp, vp, i32, vp]),
@@ -465,3 +468,13 @@ def unified_run(A: HostCSR, B: np.ndarray, Cout: np.ndarray, N: int, warmup: int
     v = A.view()
     check(lib().spmm_unified_run(C.byref(v), ptr(B), ptr(Cout), N, warmup, iters, C.byref(ms)), "spmm_unified_run")
     return float(ms.value)
+
+
+def unified_run_ex(A: HostCSR, B: np.ndarray, Cout: np.ndarray, N: int, device_budget: int, warmup: int,
+                   iters: int) -> tuple[float, int]:
+    """spmm_unified_run_ex: (median ms per pass, column phases used)."""
+    ms, ph = C.c_float(), C.c_int32()
+    v = A.view()
+    check(lib().spmm_unified_run_ex(C.byref(v), ptr(B), ptr(Cout), N, device_budget, warmup, iters, C.byref(ms),
+                                    C.byref(ph)), "spmm_unified_run_ex")
+    return float(ms.value), int(ph.value)

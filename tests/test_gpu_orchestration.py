@@ -55,6 +55,28 @@ def test_unified_memory_path(cuda):
     assert bits_equal(C, split_oracle(A, B))
 
 
+@pytest.mark.parametrize("want_phases", [1, 3, 8, 32])
+def test_unified_oversubscription_phases(cuda, want_phases):
+    # B (16384 x 512 FP32 = 32 MiB) against a device budget that does not hold it: B's rows
+    # move to the device one column phase at a time, the chain carries over in C. Rows are
+    # ragged (one long row), and one row is unsorted (its phases cut positions, not columns).
+    rng = np.random.default_rng(want_phases)
+    lens = rng.integers(0, 70, size=3000)
+    lens[17] = 5000
+    A = K.random_csr(3000, 16384, lens, seed=3)
+    s, e = A.row_ptr[5], A.row_ptr[6]
+    A.col_idx[s:e] = A.col_idx[s:e][::-1].copy()
+    B = K.dense(16384, 512, 4)
+    C = np.full((A.rows, 512), np.nan, np.float32)
+    rest = 4 * (A.rows + 1) + 8 * A.nnz + 4 * A.rows * 512 + 4 * 32 * A.rows + (64 << 20)
+    b_bytes = B.nbytes
+    budget = 0 if want_phases == 1 else rest + -(-b_bytes // want_phases)  # room for 1/P of B
+    ms, phases = S.unified_run_ex(A, B, C, 512, budget, 1, 2)
+    assert ms > 0 and phases == want_phases
+    if want_phases > 1:
+        assert bits_equal(C, O.spmm_csr_f32(K.to_oracle(A), B))
+
+
 @pytest.mark.parametrize("gpus", [1, 2, 8])
 def test_multigpu_row_split(cuda, gpus):
     A = S.generate_uniform_csr(8192, 8192, 0.01, 42)
