@@ -300,8 +300,8 @@ def main():
         bview = S.BsrView(Ah.rows, Ah.cols, Ah.block_rows, Ah.block_cols, Ah.num_blocks, Ah.nnz, S.ptr(brp),
                           S.ptr(bci), S.ptr(bva), S.DTYPE_F16)
 
-        def step():
-            S.bsr16(bview, B16, Cd, N, 0, stream)
+        def step(s=None):
+            S.bsr16(bview, B16, Cd, N, 0, s or stream)
 
         launches = 1
 
@@ -313,8 +313,8 @@ def main():
         csr_algo = plan.algo
         launches = plan.k_phases  # kernel launches per step
 
-        def step():
-            plan.execute(Bd, Cd, stream)
+        def step(s=None):
+            plan.execute(Bd, Cd, s or stream)
 
         # Compulsory bytes of one launch (this rank): A rows + row_ptr + all of B + C rows.
         alg_bytes = 8 * Ar.nnz + 4 * (rows_r + 1) + 4 * A.cols * N + 4 * rows_r * N
@@ -468,6 +468,40 @@ def main():
                 "frac": round(gather_gbs / resident, 4), "same_footprint_probe_gbs": round(same or 0.0, 1),
                 "probe": "load-only random 1 KB B-row fetches, L2-resident 32 MB (lib/libspmm_probe.so)"}
 
+    # ---- µs-scale configs: a CUDA graph of 100 back-to-back launches (no flush in between, so
+    # the inputs stay in L2), the launch-overhead-free figure for kernels of a few µs.
+    graph = None
+    if small and world == 1:
+        try:
+            g = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream()
+            cap.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(cap):
+                step(cap)  # warm the capture stream
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=cap):
+                for _ in range(100):
+                    step(torch.cuda.current_stream())
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(5):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                g.replay()
+                b.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b) / 100)
+            us = statistics.median(ts) * 1e3
+            graph = {"launches": 100, "us_per_launch": round(us, 3),
+                     "value": round(flops_total / (us * 1e-6) / 1e9, 1), "unit": UNIT,
+                     "l2": "warm (no flush between launches)"}
+            del g
+        except Exception as e:  # noqa: BLE001 - reported, not fatal
+            graph = {"error": str(e)[:200]}
+        code, detail = S.device_error(local)
+        if code != 0:
+            raise SystemExit(f"device error {code} ({detail}) in the graph batch")
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gf, threads, med = cpu_baseline_run(A, Bh, steps=3, warmup=1)
@@ -486,6 +520,7 @@ def main():
                        "l2": "inputs larger than L2" if not small else "L2 flushed between steps",
                        "b_broadcast_ms": round(bcast_ms, 4)},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": K * launches,
+            "graph_batch": graph,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
