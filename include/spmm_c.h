@@ -250,7 +250,10 @@ void spmm_csr_plan_destroy(spmm_csr_plan* plan);
 
 /* End-to-end call on HOST buffers: copies A and B to the current device (pinned or
  * pageable host memory), computes, copies C back, synchronises `stream`. Device buffers
- * are cached by the library between calls. */
+ * are cached by the library between calls. With SPMM_CSR_ROWWARP and at least 64 MiB to move,
+ * the call is pipelined: rows in 8 nnz-balanced groups on library-owned streams, so each
+ * group's (col, val) copy, its launch and its C copy back overlap the other groups' (B first,
+ * as every group reads all of it); the result is bit-identical to the unpipelined call. */
 int spmm_csr_f32_host(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
                       int32_t algo, void* stream);
 

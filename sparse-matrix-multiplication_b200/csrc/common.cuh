@@ -59,6 +59,10 @@ struct DeviceState {
     void* h_c = nullptr;  size_t h_c_bytes = 0;
     // Result flags of the device CSR -> BSR conversion.
     void* conv_flags = nullptr; size_t conv_flags_bytes = 0;
+    // Copy-in, compute and copy-out streams and their events for the pipelined host-buffer
+    // entry point (created on first use, non-blocking).
+    cudaStream_t pipe_in = nullptr, pipe_k = nullptr, pipe_out = nullptr;
+    cudaEvent_t pipe_ev[2 * 16 + 2] = {};
     std::mutex mu;
 };
 

@@ -117,6 +117,78 @@ bool check_host_view(const spmm_csr_view* A) {
            (A->nnz == 0 || (A->col_idx && A->values));
 }
 
+// Host-buffer calls moving at least this many bytes over PCIe are pipelined (ROWWARP only:
+// its result does not depend on how the rows are grouped into launches).
+constexpr size_t kPipelineBytes = 64ull << 20;
+constexpr int kPipeChunks = 8;
+
+int ensure_pipe(DeviceState* st) {
+    if (st->pipe_in) return SPMM_OK;
+    SPMM_CUDA_TRY(cudaStreamCreateWithFlags(&st->pipe_in, cudaStreamNonBlocking));
+    SPMM_CUDA_TRY(cudaStreamCreateWithFlags(&st->pipe_k, cudaStreamNonBlocking));
+    SPMM_CUDA_TRY(cudaStreamCreateWithFlags(&st->pipe_out, cudaStreamNonBlocking));
+    for (auto& e : st->pipe_ev) SPMM_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    return SPMM_OK;
+}
+
+// spmm_csr_f32_host, pipelined: rows in kPipeChunks nnz-balanced groups; the copy-in stream
+// moves row_ptr and B, then each group's (col, val) range; the compute stream runs a group's
+// ROWWARP launch as soon as its pairs have landed; the copy-out stream returns its C rows
+// while later groups are still arriving. So host -> device and device -> host transfers and the
+// kernels overlap instead of running one after another. The caller's stream is joined at both
+// ends (the work starts after what `s` already holds, and `s` waits for the last copy).
+int csr_host_pipelined(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, cudaStream_t s,
+                       DeviceState* st) {
+    SPMM_TRY(ensure_pipe(st));
+    const size_t M = hA->rows, K = hA->cols;
+    int32_t bounds[kPipeChunks + 1];
+    SPMM_TRY(spmm_nnz_balanced_bounds(hA->row_ptr, hA->rows, hA->nnz, kPipeChunks, bounds));
+    cudaEvent_t* ev = st->pipe_ev;  // [0] start, [1..16] pairs landed / launch done, [33] end
+    int* d_rp = static_cast<int*>(st->h_rp);
+    int* d_ci = static_cast<int*>(st->h_ci);
+    float* d_v = static_cast<float*>(st->h_v);
+    float* d_b = static_cast<float*>(st->h_b);
+    float* d_c = static_cast<float*>(st->h_c);
+    SPMM_CUDA_TRY(cudaEventRecord(ev[0], s));
+    SPMM_CUDA_TRY(cudaStreamWaitEvent(st->pipe_in, ev[0], 0));
+    SPMM_CUDA_TRY(cudaStreamWaitEvent(st->pipe_k, ev[0], 0));
+    SPMM_CUDA_TRY(cudaStreamWaitEvent(st->pipe_out, ev[0], 0));
+    SPMM_CUDA_TRY(cudaMemcpyAsync(d_rp, hA->row_ptr, sizeof(int) * (M + 1), cudaMemcpyHostToDevice, st->pipe_in));
+    if (K * N != 0) SPMM_CUDA_TRY(cudaMemcpyAsync(d_b, hB, sizeof(float) * K * N, cudaMemcpyHostToDevice, st->pipe_in));
+    for (int g = 0; g < kPipeChunks; ++g) {
+        const int r0 = bounds[g], r1 = bounds[g + 1];
+        const size_t p0 = static_cast<size_t>(hA->row_ptr[r0]), p1 = static_cast<size_t>(hA->row_ptr[r1]);
+        if (p1 > p0) {
+            SPMM_CUDA_TRY(cudaMemcpyAsync(d_ci + p0, hA->col_idx + p0, sizeof(int) * (p1 - p0), cudaMemcpyHostToDevice,
+                                          st->pipe_in));
+            SPMM_CUDA_TRY(cudaMemcpyAsync(d_v + p0, hA->values + p0, sizeof(float) * (p1 - p0),
+                                          cudaMemcpyHostToDevice, st->pipe_in));
+        }
+        SPMM_CUDA_TRY(cudaEventRecord(ev[1 + g], st->pipe_in));
+        SPMM_CUDA_TRY(cudaStreamWaitEvent(st->pipe_k, ev[1 + g], 0));
+        if (r1 > r0) {
+            // Rows r0..r1 as their own view: row_ptr keeps absolute positions into the arrays.
+            spmm_csr_view part = *hA;
+            part.rows = r1 - r0;
+            part.row_ptr = d_rp + r0;
+            part.col_idx = d_ci;
+            part.values = d_v;
+            SPMM_TRY(csr_f32_launch(&part, d_b, d_c + static_cast<size_t>(r0) * N, N, SPMM_CSR_ROWWARP, nullptr,
+                                    nullptr, 0, st->pipe_k, st));
+        }
+        SPMM_CUDA_TRY(cudaEventRecord(ev[1 + kPipeChunks + g], st->pipe_k));
+        SPMM_CUDA_TRY(cudaStreamWaitEvent(st->pipe_out, ev[1 + kPipeChunks + g], 0));
+        if (r1 > r0)
+            SPMM_CUDA_TRY(cudaMemcpyAsync(hC + static_cast<size_t>(r0) * N, d_c + static_cast<size_t>(r0) * N,
+                                          sizeof(float) * static_cast<size_t>(r1 - r0) * N, cudaMemcpyDeviceToHost,
+                                          st->pipe_out));
+    }
+    SPMM_CUDA_TRY(cudaEventRecord(ev[1 + 2 * kPipeChunks], st->pipe_out));
+    SPMM_CUDA_TRY(cudaStreamWaitEvent(s, ev[1 + 2 * kPipeChunks], 0));
+    SPMM_CUDA_TRY(cudaStreamSynchronize(s));
+    return SPMM_OK;
+}
+
 }  // namespace
 
 int bsr16_launch(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, int32_t algo, cudaStream_t s,
@@ -144,6 +216,9 @@ int spmm_csr_f32_host(const spmm_csr_view* hA, const float* hB, float* hC, int32
     SPMM_TRY(ensure_device_buffer(&st->h_b, &st->h_b_bytes, sizeof(float) * std::max<size_t>(K * N, 1), false, s));
     SPMM_TRY(ensure_device_buffer(&st->h_c, &st->h_c_bytes, sizeof(float) * std::max<size_t>(M * N, 1), false, s));
     SPMM_TRY(ensure_device_buffer(&st->csr_ws, &st->csr_ws_bytes, ws, true, s));
+    const size_t traffic = sizeof(int) * (M + 1) + 8 * nnz + sizeof(float) * (K * N + M * N);
+    if (algo == SPMM_CSR_ROWWARP && traffic >= kPipelineBytes && M >= 2 * kPipeChunks && N > 0)
+        return csr_host_pipelined(hA, hB, hC, N, s, st);
     SPMM_CUDA_TRY(cudaMemcpyAsync(st->h_rp, hA->row_ptr, sizeof(int) * (M + 1), cudaMemcpyHostToDevice, s));
     if (nnz) {
         SPMM_CUDA_TRY(cudaMemcpyAsync(st->h_ci, hA->col_idx, sizeof(int) * nnz, cudaMemcpyHostToDevice, s));

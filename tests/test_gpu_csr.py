@@ -182,6 +182,27 @@ def test_host_buffer_entry_point(cuda):
     assert bits_equal(C2, C)
 
 
+def test_host_buffer_pipelined_rowwarp(cuda):
+    # Large enough (> 64 MiB over PCIe) for the pipelined host path: rows in 8 groups whose
+    # copies, launches and copies back overlap. Same bits as the device-buffer call.
+    torch = cuda
+    A = S.generate_uniform_csr_fast(65536, 65536, 0.0005, 7)
+    B = K.dense(65536, 256, 8)
+    pin = lambda a: torch.from_numpy(a).pin_memory().numpy()  # noqa: E731
+    hA = S.HostCSR(A.rows, A.cols, pin(A.row_ptr), pin(A.col_idx), pin(A.values))
+    hB = pin(B)
+    hC = torch.full((A.rows, 256), float("nan")).pin_memory().numpy()
+    S.csr_f32_host(hA, hB, hC, 256, S.CSR_ROWWARP)
+    want = run(cuda, A, B, S.CSR_ROWWARP)
+    assert bits_equal(hC, want)
+    for r0 in (0, 40000):
+        sl = S.row_slice(A, r0, r0 + 256)
+        assert bits_equal(hC[r0:r0 + 256], O.spmm_csr_f32(K.to_oracle(sl), B))
+    C2 = np.full_like(want, np.nan)  # pageable output, second call on cached buffers
+    S.csr_f32_host(A, B, C2, 256, S.CSR_ROWWARP)
+    assert bits_equal(C2, want)
+
+
 @pytest.mark.parametrize("name,expect_algo", [("c1", S.CSR_ROWWARP), ("c2", S.CSR_ROWWARP), ("c4", S.CSR_MERGE)])
 def test_plan_picks_distribution_and_matches(cuda, name, expect_algo):
     torch = cuda
