@@ -266,6 +266,22 @@ int spmm_convert_f32(const float* src, uint16_t* dst, int64_t n, int32_t dtype, 
  * (reference: src/kernels/spmm_wmma.h:39, spmm_wmma) */
 int spmm_bsr16(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, void* stream);
 
+/* Inspector / executor form of spmm_bsr16 (no counterpart in the reference). Plan creation
+ * (synchronises `stream`) merges, once, the block-column lists of every group of block-rows a
+ * tensor-core CTA handles and stores the result as a fixed-stride schedule in device memory
+ * (at most 256 MiB; larger schedules, or operands the tensor-core path does not take, leave the
+ * plan on the per-call path). Execution then skips the row-pointer and column-list reads and the
+ * merge, one dependent memory round trip and a serial loop fewer per CTA. A's arrays must stay
+ * valid and unchanged; B16 and C may change per call. Same results as spmm_bsr16. */
+typedef struct spmm_bsr_plan spmm_bsr_plan;
+int spmm_bsr16_plan_create(const spmm_bsr_view* A, int32_t N, void* stream, spmm_bsr_plan** plan);
+int spmm_bsr16_plan_execute(const spmm_bsr_plan* plan, const void* B16, float* C, void* stream);
+/* Block-rows per CTA (0 = not on the tensor-core path), schedule steps of the longest group,
+ * schedule bytes (0 = no schedule). */
+int spmm_bsr16_plan_info(const spmm_bsr_plan* plan, int32_t* group, int32_t* max_steps,
+                         size_t* schedule_bytes);
+void spmm_bsr16_plan_destroy(spmm_bsr_plan* plan);
+
 /* BSR-16 path variants for measurement: 0 = auto, 1 = tcgen05, 2 = CUDA-core fallback. */
 int spmm_bsr16_algo(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, int32_t algo,
                     void* stream);

@@ -38,8 +38,24 @@
 #include <climits>
 #include <cstdint>
 #include <mutex>
+#include <new>
 
 #include "common.cuh"
+
+// A BSR-16 plan: the view, the tile group size, the per-CTA schedule (device memory, NULL when
+// the schedule would be too large or the tensor-core path does not apply) and A's tensor map.
+struct spmm_bsr_plan {
+    spmm_bsr_view A{};
+    int32_t N = 0;
+    int32_t group = 0;
+    int32_t max_steps = 0;
+    int32_t stride = 0;
+    int* sched = nullptr;
+    size_t sched_bytes = 0;
+    int32_t device = 0;
+    bool tc = false;
+    CUtensorMap ta{};
+};
 
 namespace spmm_b200 {
 namespace {
@@ -62,6 +78,10 @@ struct BsrArgs {
     float* __restrict__ C;
     int dtype;
     DeviceErrorRecord* err;
+    // Precomputed per-CTA schedule (plans): group g's record at sched + g * sched_stride:
+    // [steps, rows_mask, then per step: block column, row mask, G block indices].
+    const int* __restrict__ sched;
+    int sched_stride;
 };
 
 template <int G>
@@ -224,7 +244,7 @@ __device__ __forceinline__ uint32_t instr_desc(int dtype, uint32_t n) {
     return (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (0u << 16) | ((n >> 3) << 17) | ((128u >> 4) << 24);
 }
 
-template <int G>
+template <int G, bool SCHED>
 __global__ void __launch_bounds__(kTcThreads, 1)
     bsr_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_a, BsrArgs a) {
     using L = Layout<G>;
@@ -246,8 +266,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int br0 = blockIdx.x * G;
     const int n0 = blockIdx.y * 128;
 
-    // Block-row extents and the group's block-column list (prefix up to kColCache).
-    if (threadIdx.x <= G) {
+    // Block-row extents and the group's block-column list (prefix up to kColCache); with a
+    // precomputed schedule neither is needed.
+    const int* my_sched = SCHED ? a.sched + static_cast<size_t>(blockIdx.x) * a.sched_stride : nullptr;
+    if (!SCHED && threadIdx.x <= G) {
         const int br = min(br0 + static_cast<int>(threadIdx.x), a.block_rows);
         int v = __ldg(a.row_ptr + br);
         v = max(0, min(v, a.num_blocks));
@@ -265,10 +287,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 1) tmem_alloc(sbase + L::kTmem, G * 16 <= 32 ? 32 : (G * 16 <= 64 ? 64 : 128));
     __syncthreads();
     // Monotone block-row extents.
-    const int lo = rp[0];
-    int hi = lo;
-    for (int j = 1; j <= G; ++j) hi = max(hi, rp[j]);
-    for (int i = threadIdx.x; i < min(hi - lo, kColCache); i += kTcThreads) cols[i] = __ldg(a.col_idx + lo + i);
+    int lo = 0;
+    if constexpr (!SCHED) {
+        lo = rp[0];
+        int hi = lo;
+        for (int j = 1; j <= G; ++j) hi = max(hi, rp[j]);
+        for (int i = threadIdx.x; i < min(hi - lo, kColCache); i += kTcThreads) cols[i] = __ldg(a.col_idx + lo + i);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -289,17 +314,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
         }
         int cur = 0, end = 0;
-        if (lane < G) {
+        if (!SCHED && lane < G) {
             cur = rp[lane];
             end = max(cur, rp[lane + 1]);
         }
+        const int total_steps = SCHED ? __ldg(my_sched) : 0;
         int step = 0;           // steps fully issued so far
         unsigned last_issued = 0;  // stages of the last batch whose loads were issued
         int last_nb = 0;
         bool ok = true, done = false;
         while (ok && !done) {
             int nb = 0;
-            for (; nb < kStages; ++nb) {
+            if constexpr (SCHED) {
+                // The batch's entries, one per lane, straight from the schedule.
+                nb = min(kStages, total_steps - step);
+                if (lane < nb) {
+                    const int* e = my_sched + 2 + (step + lane) * (2 + G);
+                    sched_bc[lane] = __ldg(e);
+                    sched_mask[lane] = __ldg(e + 1);
+                    for (int j = 0; j < G; ++j) sched_blk[lane * G + j] = __ldg(e + 2 + j);
+                }
+                done = step + nb >= total_steps;
+            }
+            for (; !SCHED && nb < kStages; ++nb) {
                 int my = INT_MAX;
                 if (lane < G && cur < end) {
                     const int off = cur - lo;
@@ -438,6 +475,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else {
         // ---------------- epilogue: TMEM -> registers -> C
         const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int rows_mask = SCHED ? __ldg(my_sched + 1) : 0;
         const bool ok = __all_sync(kFullMask, mbar_wait(acc_bar, 0, abort_flag));
         tc_fence_after();
         const int col = n0 + q * 32 + lane;
@@ -445,7 +483,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int br = br0 + j;
             if (br >= a.block_rows) break;
             uint32_t v[16];
-            const bool has = rp[j + 1] > rp[j];
+            const bool has = SCHED ? ((rows_mask >> j) & 1) != 0 : rp[j + 1] > rp[j];
             if (ok && has) {
                 tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + 16 * j, v);
             } else {
@@ -545,20 +583,87 @@ int encode_2d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
     return r == CUDA_SUCCESS ? SPMM_OK : SPMM_ERR_INVALID_ARG;
 }
 
+int encode_b_map(CUtensorMap* tb, const BsrArgs& a) {
+    return encode_2d(tb, a.B, static_cast<uint64_t>(a.N), static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.N) * 2, 64,
+                     16, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int encode_a_map(CUtensorMap* ta, const BsrArgs& a) {
+    return encode_2d(ta, a.values, 16, static_cast<uint64_t>(a.num_blocks) * 16, 32, 16, 16, CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+template <int G, bool SCHED>
+int launch_tc_maps(const BsrArgs& a, const CUtensorMap& tb, const CUtensorMap& ta, cudaStream_t s) {
+    using L = Layout<G>;
+    // Per device (the attribute belongs to the current device's context).
+    SPMM_CUDA_TRY(
+        cudaFuncSetAttribute(bsr_tcgen05_kernel<G, SCHED>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamic));
+    const dim3 grid((a.block_rows + G - 1) / G, (a.N + 127) / 128);
+    bsr_tcgen05_kernel<G, SCHED><<<grid, kTcThreads, L::kDynamic, s>>>(tb, ta, a);
+    SPMM_CUDA_TRY(cudaGetLastError());
+    return SPMM_OK;
+}
+
 template <int G>
 int launch_tc(const BsrArgs& a, cudaStream_t s) {
     CUtensorMap tb, ta;
-    SPMM_TRY(encode_2d(&tb, a.B, static_cast<uint64_t>(a.N), static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.N) * 2, 64,
-                       16, CU_TENSOR_MAP_SWIZZLE_128B));
-    SPMM_TRY(encode_2d(&ta, a.values, 16, static_cast<uint64_t>(a.num_blocks) * 16, 32, 16, 16,
-                       CU_TENSOR_MAP_SWIZZLE_32B));
-    using L = Layout<G>;
-    // Per device (the attribute belongs to the current device's context).
-    SPMM_CUDA_TRY(cudaFuncSetAttribute(bsr_tcgen05_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamic));
-    const dim3 grid((a.block_rows + G - 1) / G, (a.N + 127) / 128);
-    bsr_tcgen05_kernel<G><<<grid, kTcThreads, L::kDynamic, s>>>(tb, ta, a);
-    SPMM_CUDA_TRY(cudaGetLastError());
-    return SPMM_OK;
+    SPMM_TRY(encode_b_map(&tb, a));
+    SPMM_TRY(encode_a_map(&ta, a));
+    return launch_tc_maps<G, false>(a, tb, ta, s);
+}
+
+// Plans: the producer's merge of G block-column lists, done once for every CTA group and
+// stored as a fixed-stride schedule (one warp per group). count != 0: only the step count
+// (atomicMax into *max_steps); else the records.
+template <int G>
+__global__ void __launch_bounds__(256) bsr_schedule_kernel(BsrArgs a, int* sched, int stride, int* max_steps,
+                                                          int count) {
+    const int lane = threadIdx.x & 31;
+    const int g = static_cast<int>((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+    const int groups = (a.block_rows + G - 1) / G;
+    if (g >= groups) return;
+    const int br0 = g * G;
+    int cur = 0, end = 0;
+    if (lane < G) {
+        const int br = min(br0 + lane, a.block_rows);
+        const int br1 = min(br0 + lane + 1, a.block_rows);
+        cur = max(0, min(__ldg(a.row_ptr + br), a.num_blocks));
+        end = max(cur, min(__ldg(a.row_ptr + br1), a.num_blocks));
+    }
+    const unsigned rows = __ballot_sync(kFullMask, lane < G && end > cur);
+    int* rec = sched + static_cast<size_t>(g) * stride;
+    int steps = 0;
+    for (;;) {
+        int my = INT_MAX;
+        if (lane < G && cur < end) {
+            my = __ldg(a.col_idx + cur);
+            if (my < 0 || my >= a.block_cols) {
+                if (count) record_device_error(a.err, SPMM_ERR_BAD_INDEX, cur);
+                my = max(0, min(my, a.block_cols - 1));
+            }
+        }
+        const int bc = __reduce_min_sync(kFullMask, my);
+        if (bc == INT_MAX) break;
+        const unsigned mask = __ballot_sync(kFullMask, lane < G && my == bc);
+        if (!count) {
+            int* e = rec + 2 + steps * (2 + G);
+            if (lane == 0) {
+                e[0] = bc;
+                e[1] = static_cast<int>(mask);
+            }
+            if (lane < G) e[2 + lane] = ((mask >> lane) & 1u) ? cur : 0;
+        }
+        if ((mask >> lane) & 1u) ++cur;
+        ++steps;
+    }
+    if (lane == 0) {
+        if (count) {
+            atomicMax(max_steps, steps);
+        } else {
+            rec[0] = steps;
+            rec[1] = static_cast<int>(rows);
+        }
+    }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -619,6 +724,123 @@ int spmm_bsr16_algo(const spmm_bsr_view* A, const void* B16, float* C, int32_t N
 
 int spmm_bsr16(const spmm_bsr_view* A, const void* B16, float* C, int32_t N, void* stream) {
     return spmm_bsr16_algo(A, B16, C, N, 0, stream);
+}
+
+int spmm_bsr16_plan_create(const spmm_bsr_view* A, int32_t N, void* stream, spmm_bsr_plan** out) {
+    if (!A || !out || N < 0 || A->rows < 0 || A->cols < 0 || A->num_blocks < 0 || A->block_rows < 0)
+        return SPMM_ERR_INVALID_ARG;
+    if (A->dtype != SPMM_DTYPE_F16 && A->dtype != SPMM_DTYPE_BF16) return SPMM_ERR_INVALID_ARG;
+    if (A->block_rows != (A->rows + 15) / 16 || A->block_cols != (A->cols + 15) / 16) return SPMM_ERR_INVALID_ARG;
+    if (A->rows > 0 && (!A->row_ptr || (A->num_blocks > 0 && (!A->col_idx || !A->values)))) return SPMM_ERR_INVALID_ARG;
+    if (A->num_blocks > (1 << 26)) return SPMM_ERR_TOO_LARGE;
+    DeviceState* st = nullptr;
+    SPMM_TRY(current_device_state(&st));
+    const cudaStream_t s = as_stream(stream);
+    spmm_bsr_plan* p = new (std::nothrow) spmm_bsr_plan();
+    if (!p) return SPMM_ERR_NO_MEMORY;
+    p->A = *A;
+    p->N = N;
+    p->device = st->device;
+    p->tc = st->cc_major == 10 && N % 8 == 0 && N > 0 && A->rows > 0 && A->num_blocks > 0 && A->cols > 0 &&
+            aligned16(A->values);
+    int rc = SPMM_OK;
+    if (p->tc) {
+        const long long ctas8 = static_cast<long long>((A->block_rows + 7) / 8) * ((N + 127) / 128);
+        p->group = ctas8 >= st->sm_count ? 8 : 4;
+        BsrArgs a{};
+        a.block_rows = A->block_rows;
+        a.block_cols = A->block_cols;
+        a.num_blocks = A->num_blocks;
+        a.row_ptr = A->row_ptr;
+        a.col_idx = A->col_idx;
+        a.values = A->values;
+        a.err = st->err;
+        rc = encode_a_map(&p->ta, a);
+        const int groups = (A->block_rows + p->group - 1) / p->group;
+        const unsigned blocks = static_cast<unsigned>((static_cast<long long>(groups) * 32 + 255) / 256);
+        int* d_max = nullptr;
+        if (rc == SPMM_OK && cudaMalloc(&d_max, sizeof(int)) != cudaSuccess) rc = SPMM_ERR_NO_MEMORY;
+        if (rc == SPMM_OK && cudaMemsetAsync(d_max, 0, sizeof(int), s) != cudaSuccess) rc = SPMM_ERR_CUDA;
+        if (rc == SPMM_OK) {
+            if (p->group == 8) bsr_schedule_kernel<8><<<blocks, 256, 0, s>>>(a, nullptr, 0, d_max, 1);
+            else bsr_schedule_kernel<4><<<blocks, 256, 0, s>>>(a, nullptr, 0, d_max, 1);
+            if (cudaGetLastError() != cudaSuccess ||
+                cudaMemcpyAsync(&p->max_steps, d_max, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+                cudaStreamSynchronize(s) != cudaSuccess)
+                rc = SPMM_ERR_CUDA;
+        }
+        cudaFree(d_max);
+        // A schedule of at most 256 MiB; beyond that the kernel merges on the fly.
+        if (rc == SPMM_OK) {
+            p->stride = 2 + p->max_steps * (2 + p->group);
+            const size_t bytes = sizeof(int) * static_cast<size_t>(groups) * static_cast<size_t>(p->stride);
+            if (bytes <= (256ull << 20)) {
+                if (cudaMalloc(&p->sched, bytes) != cudaSuccess) {
+                    rc = SPMM_ERR_NO_MEMORY;
+                } else {
+                    p->sched_bytes = bytes;
+                    if (p->group == 8) bsr_schedule_kernel<8><<<blocks, 256, 0, s>>>(a, p->sched, p->stride, nullptr, 0);
+                    else bsr_schedule_kernel<4><<<blocks, 256, 0, s>>>(a, p->sched, p->stride, nullptr, 0);
+                    if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) rc = SPMM_ERR_CUDA;
+                }
+            }
+        }
+    }
+    if (rc != SPMM_OK) {
+        cudaFree(p->sched);
+        delete p;
+        return rc;
+    }
+    *out = p;
+    return SPMM_OK;
+}
+
+int spmm_bsr16_plan_execute(const spmm_bsr_plan* p, const void* B16, float* C, void* stream) {
+    if (!p) return SPMM_ERR_INVALID_ARG;
+    DeviceState* st = nullptr;
+    SPMM_TRY(current_device_state(&st));
+    if (st->device != p->device) return SPMM_ERR_INVALID_ARG;
+    const cudaStream_t s = as_stream(stream);
+    if (!p->tc || !p->sched || !aligned16(B16)) return bsr16_launch(&p->A, B16, C, p->N, 0, s, st);
+    if (!C || !B16) return SPMM_ERR_INVALID_ARG;
+    BsrArgs a{};
+    a.M = p->A.rows;
+    a.K = p->A.cols;
+    a.N = p->N;
+    a.block_rows = p->A.block_rows;
+    a.block_cols = p->A.block_cols;
+    a.num_blocks = p->A.num_blocks;
+    a.row_ptr = p->A.row_ptr;
+    a.col_idx = p->A.col_idx;
+    a.values = p->A.values;
+    a.B = static_cast<const uint16_t*>(B16);
+    a.C = C;
+    a.dtype = p->A.dtype;
+    a.err = st->err;
+    a.sched = p->sched;
+    a.sched_stride = p->stride;
+    CUtensorMap tb;
+    SPMM_TRY(encode_b_map(&tb, a));
+    if (p->group == 8) return launch_tc_maps<8, true>(a, tb, p->ta, s);
+    return launch_tc_maps<4, true>(a, tb, p->ta, s);
+}
+
+int spmm_bsr16_plan_info(const spmm_bsr_plan* p, int32_t* group, int32_t* max_steps, size_t* schedule_bytes) {
+    if (!p) return SPMM_ERR_INVALID_ARG;
+    if (group) *group = p->tc ? p->group : 0;
+    if (max_steps) *max_steps = p->max_steps;
+    if (schedule_bytes) *schedule_bytes = p->sched_bytes;
+    return SPMM_OK;
+}
+
+void spmm_bsr16_plan_destroy(spmm_bsr_plan* p) {
+    if (!p) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(p->device);
+    cudaFree(p->sched);
+    cudaSetDevice(prev);
+    delete p;
 }
 
 }  // extern "C"

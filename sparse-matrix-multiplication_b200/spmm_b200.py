@@ -36,7 +36,8 @@ EXPORTS = [
     "spmm_csr_f32_ws", "spmm_csr_f32_chunk", "spmm_csr_f32_host", "spmm_convert_f32", "spmm_bsr16",
     "spmm_bsr16_algo", "spmm_device_error", "spmm_hybrid_default_threshold", "spmm_hybrid_choose",
     "spmm_backend_name", "spmm_hybrid_run", "spmm_gpu_count", "spmm_multigpu_run", "spmm_unified_run",
-    "spmm_unified_run_ex",
+    "spmm_unified_run_ex", "spmm_bsr16_plan_create", "spmm_bsr16_plan_execute", "spmm_bsr16_plan_info",
+    "spmm_bsr16_plan_destroy",
     "spmm_csr_f32_noalloc", "spmm_csr_to_bsr16_device_count", "spmm_csr_to_bsr16_device_fill",
     "spmm_csr_plan_create", "spmm_csr_plan_execute", "spmm_csr_plan_info", "spmm_csr_plan_destroy",
     "spmm_csr_plan_k_phases",
@@ -126,6 +127,10 @@ def lib() -> C.CDLL:
         "spmm_convert_f32": (C.c_int, [vp, vp, i64, i32, vp]),
         "spmm_bsr16": (C.c_int, [C.POINTER(BsrView), vp, vp, i32, vp]),
         "spmm_bsr16_algo": (C.c_int, [C.POINTER(BsrView), vp, vp, i32, i32, vp]),
+        "spmm_bsr16_plan_create": (C.c_int, [C.POINTER(BsrView), i32, vp, C.POINTER(vp)]),
+        "spmm_bsr16_plan_execute": (C.c_int, [vp, vp, vp, vp]),
+        "spmm_bsr16_plan_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_size_t)]),
+        "spmm_bsr16_plan_destroy": (None, [vp]),
         "spmm_device_error": (C.c_int, [i32, C.POINTER(i32), C.POINTER(i64), i32]),
         "spmm_hybrid_default_threshold": (f32, []),
         "spmm_hybrid_choose": (C.c_int, [C.POINTER(CsrView), i32, f32, C.POINTER(HybridPlan)]),
@@ -380,6 +385,34 @@ def convert_f32(src, dst, n: int, dtype: int = DTYPE_F16, stream=None) -> None:
 
 def bsr16(A: BsrView, B16, Cout, N: int, algo: int = 0, stream=None) -> None:
     check(lib().spmm_bsr16_algo(C.byref(A), ptr(B16), ptr(Cout), N, algo, stream_ptr(stream)), "spmm_bsr16")
+
+
+class BsrPlan:
+    """spmm_bsr16_plan_* wrapper: precompute the per-CTA schedule once, execute many times."""
+
+    def __init__(self, A: BsrView, N: int, stream=None):
+        self._A = A
+        self.N = N
+        h = C.c_void_p()
+        check(lib().spmm_bsr16_plan_create(C.byref(A), N, stream_ptr(stream), C.byref(h)), "spmm_bsr16_plan_create")
+        self._h = h
+        g, ms, nb = C.c_int32(), C.c_int32(), C.c_size_t()
+        check(lib().spmm_bsr16_plan_info(h, C.byref(g), C.byref(ms), C.byref(nb)), "spmm_bsr16_plan_info")
+        self.group, self.max_steps, self.schedule_bytes = int(g.value), int(ms.value), int(nb.value)
+
+    def execute(self, B16, Cout, stream=None) -> None:
+        check(lib().spmm_bsr16_plan_execute(self._h, ptr(B16), ptr(Cout), stream_ptr(stream)), "spmm_bsr16_plan_execute")
+
+    def close(self) -> None:
+        if self._h:
+            lib().spmm_bsr16_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
 
 
 class CsrPlan:

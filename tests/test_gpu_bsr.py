@@ -128,3 +128,67 @@ def test_convert_round_to_nearest_even(cuda, bf16):
         got = dst.cpu().numpy().view(np.uint16)
         want = O.to_half_bits(x[off:], bf16=bf16)
         assert np.array_equal(got, want)
+
+
+def _plan_run(torch, Hb: S.HostBSR, B16: np.ndarray, N: int):
+    dev = torch.device("cuda")
+    brp = torch.from_numpy(Hb.row_ptr).to(dev)
+    bci = torch.from_numpy(Hb.col_idx).to(dev)
+    bva = torch.from_numpy(Hb.values.view(np.int16)).to(dev)
+    Bt = torch.from_numpy(np.ascontiguousarray(B16).view(np.int16)).to(dev)
+    view = Hb.view()
+    view.row_ptr, view.col_idx, view.values = S.ptr(brp), S.ptr(bci), S.ptr(bva)
+    plan = S.BsrPlan(view, N, stream=torch.cuda.current_stream())
+    outs = []
+    for _ in range(2):  # the schedule is reused across executions
+        Cd = torch.full((Hb.rows, N), float("nan"), device=dev)
+        plan.execute(Bt, Cd, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        outs.append(Cd.cpu().numpy())
+    code, detail = S.device_error(0)
+    assert code == 0, f"device error {code} ({detail})"
+    info = (plan.group, plan.max_steps, plan.schedule_bytes)
+    plan.close()
+    return outs, info
+
+
+@pytest.mark.parametrize("case", ["c3", "c3_bf16", "banded", "ragged_g8", "empty_groups", "n_tail"])
+def test_plan_schedule_matches_per_call(cuda, case):
+    # The precomputed per-CTA schedule gives the per-call kernel's result bit for bit.
+    dtype = S.DTYPE_BF16 if case == "c3_bf16" else S.DTYPE_F16
+    if case.startswith("c3"):
+        A, Bf = K.config("c3")
+        N = 256
+    elif case == "banded":
+        A, Bf = K.config("c2")
+        N = 128
+    elif case == "ragged_g8":
+        lens = np.random.default_rng(2).integers(0, 12, size=32768)
+        lens[::97] = 300
+        A = K.random_csr(32768, 512, lens, seed=5)
+        Bf, N = K.dense(512, 128, 6), 128
+    elif case == "empty_groups":
+        lens = np.random.default_rng(3).integers(0, 30, size=4096)
+        lens[512:1536] = 0
+        A = K.random_csr(4096, 2048, lens, seed=4)
+        Bf, N = K.dense(2048, 192, 5), 192
+    else:
+        A = K.random_csr(1000, 999, np.random.default_rng(1).integers(0, 40, size=1000), seed=9)
+        Bf, N = K.dense(999, 136, 2), 136
+    Hb = S.csr_to_bsr16(A, dtype)
+    B16 = O.to_half_bits(Bf, bf16=dtype == S.DTYPE_BF16)
+    (c0, c1), (group, steps, nbytes) = _plan_run(cuda, Hb, B16, N)
+    assert group in (4, 8) and steps > 0 and nbytes > 0
+    want = run_bsr(cuda, Hb, B16, N, algo=1)
+    assert np.array_equal(c0.view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(c1.view(np.uint32), want.view(np.uint32))
+    check_bsr(c0, Hb, B16, dtype)
+
+
+def test_plan_falls_back_off_the_tensor_core_path(cuda):
+    A = K.random_csr(64, 64, np.full(64, 8), seed=1)
+    Hb = S.csr_to_bsr16(A)
+    B16 = O.to_half_bits(K.dense(64, 20, 2))
+    (c0, _), (group, _, nbytes) = _plan_run(cuda, Hb, B16, 20)  # N % 8 != 0: CUDA-core kernel
+    assert group == 0 and nbytes == 0
+    check_bsr(c0, Hb, B16, S.DTYPE_F16)
