@@ -137,9 +137,25 @@ int ensure_pipe(DeviceState* st) {
 // while later groups are still arriving. So host -> device and device -> host transfers and the
 // kernels overlap instead of running one after another. The caller's stream is joined at both
 // ends (the work starts after what `s` already holds, and `s` waits for the last copy).
+int csr_host_pipelined_issue(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, cudaStream_t s,
+                             DeviceState* st);
+
 int csr_host_pipelined(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, cudaStream_t s,
                        DeviceState* st) {
     SPMM_TRY(ensure_pipe(st));
+    const int rc = csr_host_pipelined_issue(hA, hB, hC, N, s, st);
+    if (rc != SPMM_OK) {
+        // Whatever was queued still reads the caller's host buffers: let it finish first.
+        cudaStreamSynchronize(st->pipe_in);
+        cudaStreamSynchronize(st->pipe_k);
+        cudaStreamSynchronize(st->pipe_out);
+        cudaStreamSynchronize(s);
+    }
+    return rc;
+}
+
+int csr_host_pipelined_issue(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N, cudaStream_t s,
+                             DeviceState* st) {
     const size_t M = hA->rows, K = hA->cols;
     int32_t bounds[kPipeChunks + 1];
     SPMM_TRY(spmm_nnz_balanced_bounds(hA->row_ptr, hA->rows, hA->nnz, kPipeChunks, bounds));
