@@ -185,7 +185,9 @@ typedef struct spmm_csr_tuning {
     int32_t col_pass;
     int32_t b_policy;
     int32_t k_phases;
-    int32_t reserved[4];
+    int32_t schedule; /* merge-path chunk scheduling: 0 = auto (static), 1 = static: warp w takes
+                         chunk w, 2 = dynamic: a resident grid takes chunks from a counter */
+    int32_t reserved[3];
 } spmm_csr_tuning;
 
 /* C = A * B, FP32, on `stream`; A, B, C are device pointers. Asynchronous.

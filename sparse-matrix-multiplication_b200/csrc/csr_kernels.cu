@@ -78,6 +78,7 @@ struct CsrArgs {
     // split[phase][i]) of row i (split[-1] = row start, split[phases-1] = row end).
     int phase, phases;
     int* ksplit;         // (phases - 1) x M split positions
+    int* sched_counters; // dynamic merge schedule: [next chunk, warps done] per slab, zero between calls
     DeviceErrorRecord* err;
 };
 
@@ -457,16 +458,9 @@ __device__ __forceinline__ void long_piece(const CsrArgs& a, PairRing* ring, int
     if (lane == 0) *counter = 0;
 }
 
+// One merge-path chunk c (items [c S, (c + 1) S)) for this warp.
 template <int VEC, int R, int U, bool HINT>
-__global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(CsrArgs a) {
-    constexpr int W = 32 * VEC * R;
-    __shared__ PairRing rings[kWarpsPerCta];
-    PairRing* ring = &rings[threadIdx.x >> 5];
-    const int lane = threadIdx.x & 31;
-    const int c = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
-    if (c >= a.num_chunks) return;
-    const int col0 = blockIdx.y * W;
-    const uint64_t pol = HINT ? evict_last_policy() : 0;
+__device__ __forceinline__ void merge_chunk(const CsrArgs& a, PairRing* ring, int c, int col0, int lane, uint64_t pol) {
     const long long d0 = static_cast<long long>(c) * a.S;
     const long long d1 = min(d0 + a.S, a.items);
     const int r0 = warp_lower_bound(a, d0, lane);
@@ -495,6 +489,40 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(
         } else {
             const int p1 = static_cast<int>(min(static_cast<long long>(re), d1 - i));
             long_piece<VEC, R, U, HINT>(a, ring, i, rs, re, rs, max(p1, rs), 2 * c + 1, col0, lane, pol);
+        }
+    }
+}
+
+// DYN = false: warp w of the grid takes chunk w. DYN = true: a persistent grid whose warps
+// take chunks from a per-slab work counter until none is left (chunks of unequal cost no
+// longer leave SMs idle at the end); the last warp to leave resets the counters. Which warp
+// runs a chunk does not change any result.
+template <int VEC, int R, int U, bool HINT, bool DYN>
+__global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(CsrArgs a) {
+    constexpr int W = 32 * VEC * R;
+    __shared__ PairRing rings[kWarpsPerCta];
+    PairRing* ring = &rings[threadIdx.x >> 5];
+    const int lane = threadIdx.x & 31;
+    const int col0 = blockIdx.y * W;
+    const uint64_t pol = HINT ? evict_last_policy() : 0;
+    if constexpr (!DYN) {
+        const int c = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+        if (c < a.num_chunks) merge_chunk<VEC, R, U, HINT>(a, ring, c, col0, lane, pol);
+    } else {
+        int* work = a.sched_counters + 2 * blockIdx.y;
+        for (;;) {
+            int c = 0;
+            if (lane == 0) c = atomicAdd(work, 1);
+            c = __shfl_sync(kFull, c, 0);
+            if (c >= a.num_chunks) break;
+            merge_chunk<VEC, R, U, HINT>(a, ring, c, col0, lane, pol);
+        }
+        if (lane == 0) {
+            const int warps = gridDim.x * kWarpsPerCta;
+            if (atomicAdd(work + 1, 1) == warps - 1) {
+                work[0] = 0;
+                work[1] = 0;
+            }
         }
     }
 }
@@ -584,6 +612,7 @@ int check_tune(const spmm_csr_tuning* tune) {
         return SPMM_ERR_INVALID_ARG;
     if (tune->b_policy < 0 || tune->b_policy > 2) return SPMM_ERR_INVALID_ARG;
     if (tune->k_phases < 0 || tune->k_phases > kMaxPhases) return SPMM_ERR_INVALID_ARG;
+    if (tune->schedule < 0 || tune->schedule > 2) return SPMM_ERR_INVALID_ARG;
     return SPMM_OK;
 }
 
@@ -598,7 +627,10 @@ size_t ksplit_bytes(int phases, int M) {
 // Counters for every slab the narrowest slab width (32 columns) could need, so the size does
 // not depend on the operands' alignment.
 size_t counter_bytes(long long num_chunks, int N) {
-    return align_up(static_cast<size_t>(num_chunks) * static_cast<size_t>((N + 31) / 32) * sizeof(int), 256);
+    // Arrival counters (num_chunks per possible 32-column slab), then the dynamic schedule's
+    // two counters per slab.
+    const size_t slabs = static_cast<size_t>((N + 31) / 32);
+    return align_up((static_cast<size_t>(num_chunks) + 2) * slabs * sizeof(int), 256);
 }
 
 size_t merge_workspace_bytes(long long num_chunks, int N) {
@@ -620,8 +652,14 @@ void launch_vr(int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
             else csr_rowwarp_kernel<VEC, R, U, false, false><<<grid, kThreads, 0, s>>>(a);
         }
     } else {
-        if (hint) csr_merge_kernel<VEC, R, U, true><<<grid, kThreads, 0, s>>>(a);
-        else csr_merge_kernel<VEC, R, U, false><<<grid, kThreads, 0, s>>>(a);
+        const bool dyn = a.sched_counters != nullptr;
+        if (hint) {
+            if (dyn) csr_merge_kernel<VEC, R, U, true, true><<<grid, kThreads, 0, s>>>(a);
+            else csr_merge_kernel<VEC, R, U, true, false><<<grid, kThreads, 0, s>>>(a);
+        } else {
+            if (dyn) csr_merge_kernel<VEC, R, U, false, true><<<grid, kThreads, 0, s>>>(a);
+            else csr_merge_kernel<VEC, R, U, false, false><<<grid, kThreads, 0, s>>>(a);
+        }
     }
 }
 
@@ -700,7 +738,13 @@ int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, 
         if (need > ws_bytes || (need > 0 && !ws)) return SPMM_ERR_INVALID_ARG;
         a.counters = static_cast<int*>(ws);
         a.partials = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_bytes(chunks, N));
-        grid.x = static_cast<unsigned>((chunks + kWarpsPerCta - 1) / kWarpsPerCta);
+        long long warps = chunks;
+        if (tune && tune->schedule == 2) {
+            // Persistent warps pulling chunks from a counter: one wave of resident warps.
+            a.sched_counters = a.counters + static_cast<size_t>(chunks) * ((N + 31) / 32);
+            warps = std::min<long long>(chunks, static_cast<long long>(st->sm_count) * SPMM_CSR_MIN_CTAS * kWarpsPerCta);
+        }
+        grid.x = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
     }
     launch(g, algo, a, grid, stream);
     SPMM_CUDA_TRY(cudaGetLastError());

@@ -80,7 +80,7 @@ class BsrStats(C.Structure):
 
 class CsrTuning(C.Structure):
     _fields_ = [("chunk", C.c_int32), ("col_pass", C.c_int32), ("b_policy", C.c_int32), ("k_phases", C.c_int32),
-                ("reserved", C.c_int32 * 4)]
+                ("schedule", C.c_int32), ("reserved", C.c_int32 * 3)]
 
 
 class HybridPlan(C.Structure):

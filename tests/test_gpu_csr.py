@@ -48,11 +48,11 @@ def run(torch, A: S.HostCSR, B: np.ndarray, algo=S.CSR_AUTO, tuning=None, b_off=
 
 
 def _counters_zero(ws, view, N, tuning) -> bool:
-    """The counter block (num_chunks ints per possible 32-column slab) is zero; partial slots
-    may hold data."""
+    """The counter block ((num_chunks + 2) ints per possible 32-column slab: arrival counters and
+    the dynamic schedule's two) is zero; partial slots may hold data."""
     chunk = S.csr_chunk(view, N, S.CSR_MERGE, tuning)
     chunks = (view.rows + view.nnz + chunk - 1) // chunk
-    return int(ws[: 4 * chunks * ((N + 31) // 32)].count_nonzero()) == 0
+    return int(ws[: 4 * (chunks + 2) * ((N + 31) // 32)].count_nonzero()) == 0
 
 
 def chunk_of(A: S.HostCSR, N: int, tuning=None) -> int:
@@ -105,16 +105,39 @@ def test_config4_power_law_bit_exact(cuda, algo):
     assert_parity(got, A, B, algo)
 
 
+@pytest.mark.parametrize("schedule", [1, 2])
 @pytest.mark.parametrize("chunk", [64, 96, 128, 512, 2048, 8192])
-def test_long_rows_any_chunk(cuda, chunk):
-    # Skewed rows (0 .. 3000 nonzeros) so that rows are cut into 1 .. 47 pieces.
+def test_long_rows_any_chunk(cuda, chunk, schedule):
+    # Skewed rows (0 .. 3000 nonzeros) so that rows are cut into 1 .. 47 pieces; static and
+    # dynamic (work-counter) chunk scheduling give the same bits.
     rng = np.random.default_rng(7)
     lens = rng.integers(0, 40, size=700)
     lens[[3, 100, 101, 350, 699]] = [3000, 1500, 65, 2049, 777]
     A = K.random_csr(700, 4000, lens, seed=8)
     B = K.dense(4000, 96, 9)
-    t = S.CsrTuning(chunk=chunk)
+    t = S.CsrTuning(chunk=chunk, schedule=schedule)
     assert_parity(run(cuda, A, B, S.CSR_MERGE, tuning=t), A, B, S.CSR_MERGE, tuning=t)
+
+
+@pytest.mark.parametrize("N", [128, 300])
+def test_dynamic_schedule_config4_repeated(cuda, N):
+    # Config 4 under the dynamic schedule, twice on one workspace (its counters reset), and
+    # N = 300 (two column slabs, one counter pair each).
+    A, B0 = K.config("c4")
+    B = B0 if N == 128 else K.dense(A.cols, N, 11)
+    t = S.CsrTuning(schedule=2, chunk=256)
+    torch = cuda
+    rp, ci, v = _dev(torch, A.row_ptr), _dev(torch, A.col_idx), _dev(torch, A.values)
+    view = S.device_view(A.rows, A.cols, rp, ci, v)
+    n = S.csr_workspace_size(view, N, S.CSR_MERGE, t)
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    Bd = _dev(torch, B)
+    for _ in range(2):
+        Cd = torch.full((A.rows, N), float("nan"), device="cuda")
+        S.csr_f32_ws(view, Bd, Cd, N, S.CSR_MERGE, t, ws, n, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        assert _counters_zero(ws, view, N, t), "counters back to zero after the call"
+        assert_parity(Cd.cpu().numpy(), A, B, S.CSR_MERGE, tuning=t)
 
 
 @pytest.mark.parametrize("N", [1, 2, 3, 8, 16, 31, 32, 33, 48, 64, 96, 100, 128, 160, 255, 256, 257, 384, 512, 1000])
