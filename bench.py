@@ -2,28 +2,36 @@
 """Benchmark of the B200 SpMM engine on BASELINE config 5 (the metric's 1/2/4/8-GPU config).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5|c1|c2|c3|c4] [--impl ours|reference]
+                    [--rank-slice R/G]
 
 Workload (default c5): A = generate_uniform_random_csr(131072, 131072, 0.001, seed 42)
 (~17.2M nnz, the reference generator's exact matrix), B = 131072 x 256 FP32 U(-1,1) from
-mt19937(43), C = A @ B in FP32. At N GPUs (one process per GPU, torchrun) A is split into
-nnz-balanced row ranges (the reference's partition), B is broadcast once from rank 0 with
-NCCL, and each rank computes its rows of C -- the total work is fixed ("strong" scaling).
+mt19937(43), C = A @ B in FP32. At N GPUs (one process per GPU, torchrun) every rank runs the
+library's per-rank multi-GPU path (spmm_rank_plan_* / spmm_rank_run of include/spmm_c.h): A is
+split into the reference's nnz-balanced row ranges, B reaches every GPU by an NCCL all-gather
+over NVLink, and each rank computes its rows of C -- the total work is fixed ("strong" scaling).
 
-One step = one SpMM of the rank's row range, inputs resident in HBM. `value` is whole-job
-GFLOP/s, 2*nnz*N / (max over ranks of the device time of the K timed steps / K). The inputs
-(406 MB at N=1) are larger than the 126 MB L2, so no flush is needed between steps.
-`e2e` repeats the measurement from pinned host buffers. At one GPU through the host-buffer
-C entry point (spmm_csr_f32_host): per step, host->device copies of A and B, the kernel, and
-the device->host copy of C. At N GPUs: per step every rank copies its A rows in, B crosses the
-host links once in total (each rank copies 1/N of its rows, then an NCCL all-gather over
-NVLink), every rank runs its plan and copies its C rows out.
+One step = one SpMM of the rank's row range, inputs resident in HBM (spmm_rank_execute). `value`
+is whole-job GFLOP/s, 2*nnz*N / (max over ranks of the device time of the K timed steps / K).
+The inputs (406 MB at N=1) are larger than the 126 MB L2, so no flush is needed between steps.
+`e2e` is the same metric through spmm_rank_run on pinned host buffers: per step, every rank copies
+its rows of A and its 1/N share of B's rows in, the ranks all-gather B over NVLink, the kernels
+run and each rank's rows of C come back -- pipelined inside the library. Both are timed with CUDA
+events on the launching stream, max over ranks.
+
+After the timed regions every rank checks its rows of C from the last end-to-end step against the
+CPU oracle (sampled rows, bit for bit) and the line carries `parity`.
 
 `roofline` carries the HBM fraction of the compulsory bytes (the reference's roofline model)
 and, for the CSR kernels, `gather_ceiling`: the rate at which the kernel pulls B rows into the
 SMs against a load-only probe of random 1 KB row fetches from an L2-resident part of B.
 
+`--rank-slice R/G` runs rank R's rows of a G-way split alone on one GPU (the same kernel launch
+that rank runs at G GPUs), to profile a rank's launch with ncu on a single GPU.
+
 `--impl reference` times the reference's CSR x dense semantics on the host cores (the
-oracle's OpenMP port: the reference ships no CPU SpMM of its own) on rank 0 only.
+oracle's OpenMP port: the reference ships no CPU SpMM of its own) on rank 0 only, on inputs made
+by the oracle's own generators.
 """
 from __future__ import annotations
 
@@ -55,6 +63,10 @@ CONFIGS = {
     "c3": "block-diagonal 8192^2 (64 dense 128^2 blocks) BSR-16 FP16, N=256, FP32 accumulate",
     "c4": "power-law CSR 16384^2 mean 164 alpha 1.8, N=128, FP32",
 }
+# (rows, cols, N) of every config, for the config dict both arms print.
+SHAPES = {"c1": (4096, 4096, 64), "c2": (8192, 8192, 128), "c3": (8192, 8192, 256), "c4": (16384, 16384, 128),
+          "c5": (131072, 131072, 256)}
+PARITY_ROWS = 1024  # sampled rows per rank checked against the oracle after timing
 
 
 def parse():
@@ -64,6 +76,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--config", default="c5", choices=sorted(CONFIGS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--rank-slice", default=None, help="R/G: rank R's rows of a G-way split, alone on one GPU")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-clocks", action="store_true")
@@ -72,6 +85,14 @@ def parse():
         p.error("--warmup must be >= 3")
     if a.steps is None:
         a.steps = 400 if a.config == "c5" else 200
+    if a.rank_slice is not None:
+        try:
+            r, g = (int(x) for x in a.rank_slice.split("/"))
+        except ValueError:
+            p.error("--rank-slice wants R/G")
+        if not (0 <= r < g) or a.config == "c3":
+            p.error("--rank-slice wants 0 <= R < G and a CSR config")
+        a.rank_slice = (r, g)
     return a
 
 
@@ -84,6 +105,16 @@ def peaks():
         except (ValueError, KeyError):
             pass
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def config_dict(cfg: str, nnz: int, world: int, small: bool, rank_slice=None) -> dict:
+    """The workload description; both arms print the same dict."""
+    rows, cols, n = SHAPES[cfg]
+    par = f"row-split x{world} (nnz-balanced)"
+    if rank_slice is not None:
+        par = f"rank {rank_slice[0]} of a {rank_slice[1]}-way row split, alone on one GPU"
+    return {"workload": CONFIGS[cfg], "config_id": cfg, "nnz": int(nnz), "N": n, "rows": rows, "cols": cols,
+            "parallelism": par, "l2": "L2 flushed between steps" if small else "inputs larger than L2"}
 
 
 # ------------------------------------------------------------------------ inputs
@@ -153,29 +184,29 @@ class Clocks:
 # ------------------------------------------------------------------------ gather ceiling
 
 
-def gather_ceiling(torch, Bd, rows: int, fetches: int, stream) -> float | None:
-    """Random whole-row gather rate (GB/s) of this GPU over the first `rows` rows of Bd
-    (N = 256 only): lib/libspmm_probe.so, same residency and load width as the CSR kernels,
-    no arithmetic. The median of 5 launches of `fetches` 1 KB rows each."""
+def gather_ceiling(torch, b_ptr: int, n_cols: int, rows: int, fetches: int, stream) -> float | None:
+    """Random whole-row gather rate (GB/s) of this GPU over the first `rows` rows of the device B
+    at b_ptr (N = 256 only): lib/libspmm_probe.so, same residency and load width as the CSR
+    kernels, no arithmetic. The median of 5 launches of `fetches` 1 KB rows each."""
     import ctypes as C
 
     so = PKG / "lib" / "libspmm_probe.so"
-    if Bd.shape[1] != 256 or not so.exists() or fetches < 4:
+    if n_cols != 256 or not so.exists() or fetches < 4:
         return None
     lib = C.CDLL(str(so))
     lib.spmm_probe_gather.argtypes = [C.c_void_p, C.c_uint32, C.c_longlong, C.c_uint32, C.c_void_p, C.c_void_p]
     ctas = C.c_int()
     if lib.spmm_probe_ctas(C.byref(ctas)) != 0:
         return None
-    out = torch.empty(ctas.value * 256, dtype=torch.float32, device=Bd.device)
+    out = torch.empty(ctas.value * 256, dtype=torch.float32, device="cuda")
     fetches -= fetches % 4
     ts = []
     for i in range(7):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        rc = lib.spmm_probe_gather(C.c_void_p(Bd.data_ptr()), rows, fetches, i, C.c_void_p(out.data_ptr()),
+        a.record(stream)
+        rc = lib.spmm_probe_gather(C.c_void_p(b_ptr), rows, fetches, i, C.c_void_p(out.data_ptr()),
                                    C.c_void_p(stream.cuda_stream))
-        b.record()
+        b.record(stream)
         torch.cuda.synchronize()
         if rc != 0:
             return None
@@ -184,7 +215,7 @@ def gather_ceiling(torch, Bd, rows: int, fetches: int, stream) -> float | None:
     return fetches * 1024.0 / (statistics.median(ts) * 1e-3) / 1e9
 
 
-# ------------------------------------------------------------------------ CPU baseline
+# ------------------------------------------------------------------------ CPU baseline and checker
 
 
 def cpu_baseline_run(A, B, steps: int, warmup: int):
@@ -205,7 +236,88 @@ def cpu_baseline_run(A, B, steps: int, warmup: int):
     return flops / med / 1e9, threads, med
 
 
+def parity_rows(A, B: np.ndarray, r0: int, r1: int, C_rows: np.ndarray, algo: int, chunk: int) -> tuple[int, bool]:
+    """Checker, run after the timed regions: this rank's rows of C against the CPU oracle, bit
+    for bit. One-warp-per-row plans follow the reference's sequential FMA chain per element
+    (spmm_baseline.cu:19-24), so PARITY_ROWS sampled rows are compared with oracle.spmm_csr_f32;
+    merge-path plans cut long rows at chunk boundaries of the launch, so all its rows are
+    compared with oracle.spmm_csr_f32_split. Returns (rows checked, all equal)."""
+    from oracle import oracle as O
+
+    import spmm_b200 as S
+
+    rows = r1 - r0
+    if rows == 0:
+        return 0, True
+    if algo == S.CSR_MERGE:
+        sl = S.row_slice(A, r0, r1)
+        want = O.spmm_csr_f32_split(O.CSR(sl.rows, sl.cols, sl.row_ptr, sl.col_idx, sl.values), B, chunk)
+        return rows, bool(np.array_equal(C_rows.view(np.uint32), want.view(np.uint32)))
+    rng = np.random.default_rng(1000 + r0)
+    k = min(PARITY_ROWS, rows)
+    idx = np.sort(rng.choice(rows, size=k, replace=False)) + r0
+    starts, ends = A.row_ptr[idx].astype(np.int64), A.row_ptr[idx + 1].astype(np.int64)
+    lens = ends - starts
+    sub_rp = np.zeros(k + 1, np.int32)
+    np.cumsum(lens, out=sub_rp[1:])
+    sel = (np.repeat(starts - sub_rp[:-1], lens) + np.arange(int(lens.sum()))).astype(np.int64)
+    sub = O.CSR(k, A.cols, sub_rp, np.ascontiguousarray(A.col_idx[sel]), np.ascontiguousarray(A.values[sel]))
+    want = O.spmm_csr_f32(sub, B)
+    got = np.ascontiguousarray(C_rows[idx - r0])
+    return k, bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+
+
 # ------------------------------------------------------------------------ main
+
+
+class Ranks:
+    """torch.distributed helpers: barrier, max / sum / min over ranks (no-ops at one rank)."""
+
+    def __init__(self, torch, dist, world: int):
+        self.torch, self.dist, self.world = torch, dist, world
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def _reduce(self, x: float, op) -> float:
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    def max(self, x: float) -> float:
+        return self._reduce(x, self.dist.ReduceOp.MAX)
+
+    def sum(self, x: float) -> float:
+        return self._reduce(x, self.dist.ReduceOp.SUM)
+
+    def min(self, x: float) -> float:
+        return self._reduce(x, self.dist.ReduceOp.MIN)
+
+
+def time_steps(torch, step, K: int, stream, flush, R: Ranks):
+    """K steps on `stream`, each bracketed by CUDA events; the region bracketed by a barrier and
+    a synchronize on both sides. Returns (ms per step: region / K, or the sum of the per-step
+    times when an L2 flush runs between steps; average per-step ms)."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    R.barrier()
+    torch.cuda.synchronize()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(K):
+        if flush is not None:
+            flush.fill_(float(i))  # L2 flush between steps (inputs smaller than L2)
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    R.barrier()
+    per = [a.elapsed_time(b) for a, b in evs]
+    region = sum(per) if flush is not None else t_start.elapsed_time(t_end)
+    return region / K, sum(per) / K
 
 
 def main():
@@ -218,6 +330,8 @@ def main():
     cfg_name = args.config
     if world > 1 and cfg_name != "c5":
         raise SystemExit("only config c5 is sharded across GPUs")
+    if world > 1 and args.rank_slice is not None:
+        raise SystemExit("--rank-slice runs on one GPU")
 
     if args.impl == "reference":
         return run_reference(args, rank, world)
@@ -225,106 +339,76 @@ def main():
     import torch
     import torch.distributed as dist
 
-    import spmm_b200 as S
-
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-
-    def barrier():
+    R = Ranks(torch, dist, world)
+    try:
+        line = (run_bsr if cfg_name == "c3" else run_csr)(args, torch, dist, R, rank, world, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
         if world > 1:
             dist.barrier()
+            dist.destroy_process_group()
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
-    def sum_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+def run_csr(args, torch, dist, R: Ranks, rank: int, world: int, local: int) -> dict:
+    import spmm_b200 as S
 
+    cfg_name = args.config
     A, Bh = build_inputs(cfg_name)
+    full_nnz = A.nnz
+    if args.rank_slice is not None:
+        sr, sg = args.rank_slice
+        b = S.nnz_balanced_bounds(A.row_ptr, A.rows, A.nnz, sg)
+        A = S.row_slice(A, int(b[sr]), int(b[sr + 1]))
     N = Bh.shape[1]
-    total_nnz = A.nnz
-    flops_total = 2.0 * total_nnz * N
+    flops_total = 2.0 * A.nnz * N
     hbm_peak, tc_peak, peak_src = peaks()
     stream = torch.cuda.current_stream()
-
-    # ---- this rank's rows: the reference's nnz-balanced partition
-    bounds = S.nnz_balanced_bounds(A.row_ptr, A.rows, A.nnz, world)
-    r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
-    Ar = S.row_slice(A, r0, r1)
-    rows_r = r1 - r0
-
-    dev = torch.device("cuda", local)
-    rp = torch.from_numpy(Ar.row_ptr).to(dev)
-    ci = torch.from_numpy(Ar.col_idx).to(dev)
-    va = torch.from_numpy(Ar.values).to(dev)
-    # B: host -> rank 0, then NCCL broadcast over NVLink (timed separately, outside `value`).
-    Bd = torch.empty((A.cols, N), dtype=torch.float32, device=dev)
-    if rank == 0:
-        Bd.copy_(torch.from_numpy(Bh))
-    torch.cuda.synchronize()
-    bcast_ms = 0.0
-    if world > 1:
-        warm = torch.zeros(1024, dtype=torch.float32, device=dev)
-        dist.broadcast(warm, src=0)  # communicator set-up stays out of the timed broadcast
-        torch.cuda.synchronize()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        dist.broadcast(Bd, src=0)
-        e1.record()
-        torch.cuda.synchronize()
-        bcast_ms = max_over_ranks(e0.elapsed_time(e1))
-    Cd = torch.empty((max(rows_r, 1), N), dtype=torch.float32, device=dev)
-    view = S.device_view(rows_r, A.cols, rp, ci, va)
     small = cfg_name != "c5"
 
-    # ---- kernel step
-    if cfg_name == "c3":
-        Ah = S.csr_to_bsr16(A, S.DTYPE_F16)
-        brp = torch.from_numpy(Ah.row_ptr).to(dev)
-        bci = torch.from_numpy(Ah.col_idx).to(dev)
-        bva = torch.from_numpy(Ah.values.view(np.int16)).to(dev)
-        B16 = torch.empty((A.cols, N), dtype=torch.float16, device=dev)
-        S.convert_f32(Bd, B16, A.cols * N, S.DTYPE_F16, stream)
-        bview = S.BsrView(Ah.rows, Ah.cols, Ah.block_rows, Ah.block_cols, Ah.num_blocks, Ah.nnz, S.ptr(brp),
-                          S.ptr(bci), S.ptr(bva), S.DTYPE_F16)
+    # Pinned host operands: A's arrays, B, and this rank's rows of C.
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()  # noqa: E731
+    hA = S.HostCSR(A.rows, A.cols, pin(A.row_ptr), pin(A.col_idx), pin(A.values))
+    hB = pin(Bh)
 
-        # Inspect A once (the per-CTA schedule of the tensor-core kernel).
-        bplan = S.BsrPlan(bview, N, stream=stream)
+    # ---- the library's per-rank path: communicator (N > 1), plan, one end-to-end run to load
+    comm = None
+    if world > 1:
+        obj = [S.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = S.RankComm(obj[0], world, rank, timeout_ms=120000)
+    plan = S.RankPlan(comm, hA, N, stream)
+    r0, r1 = plan.row_begin, plan.row_end
+    rows_r = r1 - r0
+    hC = torch.empty((max(rows_r, 1), N), dtype=torch.float32).pin_memory().numpy()
+    plan.run(hA, hB, hC, stream)
+    torch.cuda.synchronize()
+    kernel_name = "csr_rowwarp_kernel" if plan.algo == S.CSR_ROWWARP else "csr_merge_kernel"
+    chunk = S.csr_chunk(S.CsrView(rows_r, A.cols, plan.nnz, 0, 0, 0), N) if plan.algo == S.CSR_MERGE else 0
 
-        def step(s=None):
-            bplan.execute(B16, Cd, s or stream)
+    gather_ms = None
+    if world > 1:
+        ts = []
+        for i in range(6):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            R.barrier()
+            a.record(stream)
+            plan.gather_b(stream)
+            b.record(stream)
+            torch.cuda.synchronize()
+            if i:
+                ts.append(a.elapsed_time(b))
+        gather_ms = R.max(statistics.median(ts))
 
-        launches = 1
+    def step(s=None):
+        plan.execute(s or stream)
 
-        alg_bytes = 512 * Ah.num_blocks + 4 * Ah.num_blocks + 4 * (Ah.block_rows + 1) + 2 * A.cols * N + 4 * A.rows * N
-        kernel_name = "bsr_tcgen05_kernel"
-    else:
-        # Inspect the rank's rows once (picks the work distribution, owns the workspace).
-        plan = S.CsrPlan(view, N, stream=stream)
-        csr_algo = plan.algo
-        launches = plan.k_phases  # kernel launches per step
-
-        def step(s=None):
-            plan.execute(Bd, Cd, s or stream)
-
-        # Compulsory bytes of one launch (this rank): A rows + row_ptr + all of B + C rows.
-        alg_bytes = 8 * Ar.nnz + 4 * (rows_r + 1) + 4 * A.cols * N + 4 * rows_r * N
-        kernel_name = "csr_rowwarp_kernel" if csr_algo == S.CSR_ROWWARP else "csr_merge_kernel"
-
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev) if small else None
-
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda") if small else None
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -332,228 +416,288 @@ def main():
     if code != 0:
         raise SystemExit(f"device error {code} ({detail}) during warm-up")
 
-    # ---- timed region
+    # ---- timed region: kernels on resident operands
     clocks = Clocks(local, enabled=not args.no_clocks)
     clocks.start()
     K = args.steps
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    barrier()
-    torch.cuda.synchronize()
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_start.record()
-    for i in range(K):
-        if flush is not None:
-            flush.fill_(float(i))  # L2 flush between steps (inputs smaller than L2)
-        evs[i][0].record()
-        step()
-        evs[i][1].record()
-    t_end.record()
-    torch.cuda.synchronize()
-    barrier()
+    ms_rank, avg_launch_ms = time_steps(torch, step, K, stream, flush, R)
     clk = clocks.stop()
-    per_launch = [a.elapsed_time(b) for a, b in evs]
-    if small:
-        region_ms = sum(per_launch)  # flushes excluded
+    ms_step = R.max(ms_rank)
+    code, detail = S.device_error(local)
+    if code != 0:
+        raise SystemExit(f"device error {code} ({detail}) in the timed region")
+    total_flops = 2.0 * R.sum(float(plan.nnz)) * N
+    value = total_flops / (ms_step * 1e-3) / 1e9
+
+    # ---- end to end through spmm_rank_run (host buffers, copies inside the timed region)
+    e2e = None
+    if not args.no_e2e:
+        for _ in range(2):
+            plan.run(hA, hB, hC, stream)
+        ke = max(3, min(K, 20))
+        ms_e2e_rank, _ = time_steps(torch, lambda: plan.run(hA, hB, hC, stream), ke, stream, None, R)
+        e2e_ms = R.max(ms_e2e_rank)
+        h2d = R.sum(float(4 * (rows_r + 1) + 8 * plan.nnz + 4 * (plan.b_row_end - plan.b_row_begin) * N))
+        d2h = R.sum(float(4 * rows_r * N))
+        e2e = {"value": round(total_flops / (e2e_ms * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "api": "spmm_rank_run (C ABI; per rank: its A rows and 1/N of B's rows H2D from pinned buffers, "
+                      "NCCL all-gather of B over NVLink, kernels, its C rows D2H; pipelined in row groups)"}
     else:
-        region_ms = t_start.elapsed_time(t_end)
-    ms_step = max_over_ranks(region_ms / K)
-    avg_launch_ms = sum(per_launch) / K
+        plan.run(hA, hB, hC, stream)
+    torch.cuda.synchronize()
+
+    # ---- parity of this rank's rows (checker, after timing)
+    checked, ok = parity_rows(A, Bh, r0, r1, hC[:rows_r], plan.algo, chunk)
+    parity = {"rows_checked": int(R.sum(float(checked))), "ok": bool(R.min(1.0 if ok else 0.0) == 1.0),
+              "ranks": world, "bitwise": True,
+              "oracle": ("oracle.spmm_csr_f32 (sequential FMA chain per element), sampled rows per rank"
+                         if plan.algo == S.CSR_ROWWARP else "oracle.spmm_csr_f32_split (merge-path cut), all rows"),
+              "source": "C rows of the last end-to-end step (host)"}
+
+    # ---- roofline of the dominant kernel (per launch, this rank; rank 0 reports)
+    alg_bytes = 8 * plan.nnz + 4 * (rows_r + 1) + 4 * A.cols * N + 4 * rows_r * N
+    launches = max(plan.launches, 1)
+    achieved = alg_bytes / (avg_launch_ms * 1e-3) / 1e9
+    gpus_key = args.rank_slice[1] if args.rank_slice is not None else world
+    traffic = None
+    prof = REPO / "profiles" / f"{kernel_name}_config{cfg_name[1:]}.md"
+    if prof.exists():
+        key = f"dram_bytes_per_launch_gpus{gpus_key}:"
+        for ln in prof.read_text().splitlines():
+            if ln.startswith(key):
+                traffic = int(ln.split(":", 1)[1].strip())
+    roofline = {"bound": "hbm", "kernel": kernel_name, "achieved": round(achieved, 1), "peak": hbm_peak,
+                "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
+                "alg_bytes_per_launch": int(alg_bytes), "avg_launch_ms": round(avg_launch_ms, 5)}
+    gathered = 4.0 * plan.nnz * N  # B-row bytes the gather moves through L2 per launch
+    gather_gbs = gathered / (avg_launch_ms * 1e-3) / 1e9
+    roofline["l2_gather_gbs"] = round(gather_gbs, 1)
+    # The ceiling that bounds a gather of whole B rows: a load-only probe that pulls random
+    # 1 KB rows into the SMs from an L2-resident 32 MB part of B, and the same probe over B's
+    # whole footprint (uniformly random rows, so it misses L2 more often than the kernel, whose
+    # warps walk their sorted columns together).
+    resident = gather_ceiling(torch, plan.d_B, N, min(A.cols, 32768), plan.nnz, stream)
+    same = gather_ceiling(torch, plan.d_B, N, A.cols, plan.nnz, stream)
+    if resident:
+        roofline["gather_ceiling"] = {
+            "achieved_gbs": round(gather_gbs, 1), "ceiling_gbs": round(resident, 1),
+            "frac": round(gather_gbs / resident, 4), "same_footprint_probe_gbs": round(same or 0.0, 1),
+            "probe": "load-only random 1 KB B-row fetches, L2-resident 32 MB (lib/libspmm_probe.so)"}
+
+    graph = graph_batch(torch, step, flops_total, S, local) if small and world == 1 else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.rank_slice is None:
+        gf, threads, med = cpu_baseline_run(A, Bh, steps=3, warmup=1)
+        cpu = {"value": round(gf, 3), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"full {cfg_name} product, median of 3 (OpenMP static over rows, {med*1e3:.0f} ms each)"}
+
+    path = {"api": "spmm_rank_plan_create / spmm_rank_execute (C ABI)", "kernel": kernel_name,
+            "algo": "rowwarp" if plan.algo == S.CSR_ROWWARP else "merge", "rows_this_rank": rows_r,
+            "b_allgather_ms": round(gather_ms, 4) if gather_ms is not None else None}
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (reference generators, fixed seeds)",
+        "config": config_dict(cfg_name, A.nnz if args.rank_slice else full_nnz, world, small, args.rank_slice),
+        "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": K * launches,
+        "parity": parity, "path": path, "graph_batch": graph,
+    }
+    plan.close()
+    if comm is not None:
+        comm.close()
+    return line
+
+
+def graph_batch(torch, step, flops_total: float, S, local: int):
+    """µs-scale configs: a CUDA graph of 100 back-to-back launches (no flush in between, so the
+    inputs stay in L2), the launch-overhead-free figure for kernels of a few µs."""
+    try:
+        g = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
+            step(cap)  # warm the capture stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=cap):
+            for _ in range(100):
+                step(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) / 100)
+        us = statistics.median(ts) * 1e3
+        out = {"launches": 100, "us_per_launch": round(us, 3), "value": round(flops_total / (us * 1e-6) / 1e9, 1),
+               "unit": UNIT, "l2": "warm (no flush between launches)"}
+        del g
+    except Exception as e:  # noqa: BLE001 - reported, not fatal
+        out = {"error": str(e)[:200]}
+    code, detail = S.device_error(local)
+    if code != 0:
+        raise SystemExit(f"device error {code} ({detail}) in the graph batch")
+    return out
+
+
+def run_bsr(args, torch, dist, R: Ranks, rank: int, world: int, local: int) -> dict:
+    """Config 3: BSR-16 FP16 on the tensor cores (spmm_bsr16_plan_*), one GPU."""
+    import spmm_b200 as S
+
+    A, Bh = build_inputs("c3")
+    N = Bh.shape[1]
+    flops_total = 2.0 * A.nnz * N
+    hbm_peak, tc_peak, peak_src = peaks()
+    stream = torch.cuda.current_stream()
+    dev = torch.device("cuda", local)
+    Ah = S.csr_to_bsr16(A, S.DTYPE_F16)
+    brp = torch.from_numpy(Ah.row_ptr).to(dev)
+    bci = torch.from_numpy(Ah.col_idx).to(dev)
+    bva = torch.from_numpy(Ah.values.view(np.int16)).to(dev)
+    Bd = torch.from_numpy(Bh).to(dev)
+    B16 = torch.empty((A.cols, N), dtype=torch.float16, device=dev)
+    S.convert_f32(Bd, B16, A.cols * N, S.DTYPE_F16, stream)
+    Cd = torch.empty((A.rows, N), dtype=torch.float32, device=dev)
+    bview = S.BsrView(Ah.rows, Ah.cols, Ah.block_rows, Ah.block_cols, Ah.num_blocks, Ah.nnz, S.ptr(brp),
+                      S.ptr(bci), S.ptr(bva), S.DTYPE_F16)
+    bplan = S.BsrPlan(bview, N, stream=stream)  # the per-CTA schedule, made once
+
+    def step(s=None):
+        bplan.execute(B16, Cd, s or stream)
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    code, detail = S.device_error(local)
+    if code != 0:
+        raise SystemExit(f"device error {code} ({detail}) during warm-up")
+    clocks = Clocks(local, enabled=not args.no_clocks)
+    clocks.start()
+    K = args.steps
+    ms_step, avg_launch_ms = time_steps(torch, step, K, stream, flush, R)
+    clk = clocks.stop()
     code, detail = S.device_error(local)
     if code != 0:
         raise SystemExit(f"device error {code} ({detail}) in the timed region")
     value = flops_total / (ms_step * 1e-3) / 1e9
 
-    # ---- end to end through the host-buffer entry point
-    e2e = None
-    if not args.no_e2e and cfg_name != "c3" and world > 1:
-        # Multi-GPU end to end: every rank copies its A rows host -> device; B crosses the
-        # host links once in total -- each rank copies 1/N of B's rows and NCCL all-gathers
-        # them over NVLink (when N divides B's rows; else rank 0 copies B and broadcasts it,
-        # as spmm_multigpu does); every rank runs its plan (spmm_csr_plan_execute) and copies
-        # its C rows back.
-        pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
-        h_rp, h_ci, h_va = pin(Ar.row_ptr), pin(Ar.col_idx), pin(Ar.values)
-        gather_b = A.cols % world == 0
-        if gather_b:
-            kb = A.cols // world
-            h_b = pin(np.ascontiguousarray(Bh[rank * kb:(rank + 1) * kb]))
-            b_part = Bd[rank * kb:(rank + 1) * kb]
-        else:
-            h_b = pin(Bh) if rank == 0 else None
-        h_c = torch.empty((max(rows_r, 1), N), dtype=torch.float32).pin_memory()
+    # Checker (after timing): the whole C against the FP64 oracle on the same FP16 inputs.
+    from oracle import oracle as O
 
-        def e2e_step():
-            rp.copy_(h_rp, non_blocking=True)
-            ci.copy_(h_ci, non_blocking=True)
-            va.copy_(h_va, non_blocking=True)
-            if gather_b:
-                b_part.copy_(h_b, non_blocking=True)
-                dist.all_gather_into_tensor(Bd, b_part)
-            else:
-                if rank == 0:
-                    Bd.copy_(h_b, non_blocking=True)
-                dist.broadcast(Bd, src=0)
-            plan.execute(Bd, Cd, stream)
-            h_c.copy_(Cd, non_blocking=True)
-            torch.cuda.synchronize()
+    ob = O.BSR(Ah.rows, Ah.cols, Ah.block_rows, Ah.block_cols, Ah.row_ptr, Ah.col_idx, Ah.values, Ah.nnz)
+    ref = O.spmm_bsr_f64(ob, B16.cpu().numpy().view(np.uint16), 0)
+    err = float(np.abs(Cd.cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
+    parity = {"rows_checked": A.rows, "ok": err <= 1e-5, "max_abs_err_over_max_ref": err, "bitwise": False,
+              "oracle": "oracle.spmm_bsr_f64 on the same FP16 inputs (tolerance 1e-5 of max |ref|)", "ranks": 1}
 
-        for _ in range(2):
-            e2e_step()
-        ke = max(3, min(K, 20))
-        barrier()
-        t0 = time.perf_counter()
-        for _ in range(ke):
-            e2e_step()
-        e2e_ms = (time.perf_counter() - t0) * 1e3 / ke
-        barrier()
-        e2e_ms = max_over_ranks(e2e_ms)
-        h2d = sum_over_ranks(float(Ar.row_ptr.nbytes + Ar.col_idx.nbytes + Ar.values.nbytes)) + Bh.nbytes
-        d2h = sum_over_ranks(float(rows_r * N * 4))
-        how = "1/N of B's rows H2D + NCCL all-gather" if gather_b else "B H2D on rank 0 + NCCL broadcast"
-        e2e = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "api": f"per rank: A rows H2D, {how}, spmm_csr_plan_execute, C rows D2H"}
-    elif not args.no_e2e and cfg_name != "c3":
-        pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
-        hA = S.HostCSR(Ar.rows, Ar.cols, pin(Ar.row_ptr).numpy(), pin(Ar.col_idx).numpy(), pin(Ar.values).numpy())
-        hB = pin(Bh).numpy()
-        hC = torch.empty((max(rows_r, 1), N), dtype=torch.float32).pin_memory().numpy()
-        for _ in range(2):
-            S.csr_f32_host(hA, hB, hC, N, csr_algo, stream)
-        ke = max(3, min(K, 20))
-        barrier()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(ke):
-            S.csr_f32_host(hA, hB, hC, N, csr_algo, stream)
-        torch.cuda.synchronize()
-        e2e_ms = (time.perf_counter() - t0) * 1e3 / ke
-        barrier()
-        e2e_ms = max_over_ranks(e2e_ms)
-        h2d = sum_over_ranks(float(Ar.row_ptr.nbytes + Ar.col_idx.nbytes + Ar.values.nbytes + Bh.nbytes))
-        d2h = sum_over_ranks(float(rows_r * N * 4))
-        e2e = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "api": "spmm_csr_f32_host (C ABI, pinned host buffers)"}
-
-    # ---- roofline of the dominant kernel (per launch, this rank; rank 0 reports)
+    alg_bytes = 512 * Ah.num_blocks + 4 * Ah.num_blocks + 4 * (Ah.block_rows + 1) + 2 * A.cols * N + 4 * A.rows * N
+    kernel_name = "bsr_tcgen05_kernel"
     achieved = alg_bytes / (avg_launch_ms * 1e-3) / 1e9
-    # DRAM bytes per launch from the committed ncu summary of this kernel and config, for this
-    # GPU count (a line "dram_bytes_per_launch_gpus<N>: <bytes>"); null when not captured.
     traffic = None
-    prof = REPO / "profiles" / f"{kernel_name}_config{cfg_name[1:]}.md"
+    prof = REPO / "profiles" / f"{kernel_name}_config3.md"
     if prof.exists():
-        key = f"dram_bytes_per_launch_gpus{world}:"
-        for line in prof.read_text().splitlines():
-            if line.startswith(key):
-                traffic = int(line.split(":", 1)[1].strip())
+        for ln in prof.read_text().splitlines():
+            if ln.startswith("dram_bytes_per_launch_gpus1:"):
+                traffic = int(ln.split(":", 1)[1].strip())
+    tflops = 2.0 * A.nnz * N / (avg_launch_ms * 1e-3) / 1e12
     roofline = {"bound": "hbm", "kernel": kernel_name, "achieved": round(achieved, 1), "peak": hbm_peak,
                 "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
-                "alg_bytes_per_launch": int(alg_bytes), "avg_launch_ms": round(avg_launch_ms, 5)}
-    if cfg_name == "c3":
-        tflops = 2.0 * A.nnz * N / (avg_launch_ms * 1e-3) / 1e12
-        roofline["tensor"] = {"achieved_tflops": round(tflops, 2), "peak_tflops": tc_peak,
-                              "frac": round(tflops / tc_peak, 4)}
-    else:
-        gathered = 4.0 * Ar.nnz * N  # B-row bytes the gather moves through L2 per launch
-        gather_gbs = gathered / (avg_launch_ms * 1e-3) / 1e9
-        roofline["l2_gather_gbs"] = round(gather_gbs, 1)
-        # The ceiling that bounds a gather of whole B rows: a load-only probe that pulls random
-        # 1 KB rows into the SMs from an L2-resident 32 MB part of B (the fastest any gather can
-        # go), and the same probe over B's whole footprint (uniformly random rows, so it misses
-        # L2 more often than the kernel, whose warps walk their sorted columns together).
-        resident = gather_ceiling(torch, Bd, min(A.cols, 32768), Ar.nnz, stream)
-        same = gather_ceiling(torch, Bd, A.cols, Ar.nnz, stream)
-        if resident:
-            roofline["gather_ceiling"] = {
-                "achieved_gbs": round(gather_gbs, 1), "ceiling_gbs": round(resident, 1),
-                "frac": round(gather_gbs / resident, 4), "same_footprint_probe_gbs": round(same or 0.0, 1),
-                "probe": "load-only random 1 KB B-row fetches, L2-resident 32 MB (lib/libspmm_probe.so)"}
-
-    # ---- µs-scale configs: a CUDA graph of 100 back-to-back launches (no flush in between, so
-    # the inputs stay in L2), the launch-overhead-free figure for kernels of a few µs.
-    graph = None
-    if small and world == 1:
-        try:
-            g = torch.cuda.CUDAGraph()
-            cap = torch.cuda.Stream()
-            cap.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(cap):
-                step(cap)  # warm the capture stream
-            torch.cuda.synchronize()
-            with torch.cuda.graph(g, stream=cap):
-                for _ in range(100):
-                    step(torch.cuda.current_stream())
-            torch.cuda.synchronize()
-            ts = []
-            for _ in range(5):
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record()
-                g.replay()
-                b.record()
-                torch.cuda.synchronize()
-                ts.append(a.elapsed_time(b) / 100)
-            us = statistics.median(ts) * 1e3
-            graph = {"launches": 100, "us_per_launch": round(us, 3),
-                     "value": round(flops_total / (us * 1e-6) / 1e9, 1), "unit": UNIT,
-                     "l2": "warm (no flush between launches)"}
-            del g
-        except Exception as e:  # noqa: BLE001 - reported, not fatal
-            graph = {"error": str(e)[:200]}
-        code, detail = S.device_error(local)
-        if code != 0:
-            raise SystemExit(f"device error {code} ({detail}) in the graph batch")
-
+                "alg_bytes_per_launch": int(alg_bytes), "avg_launch_ms": round(avg_launch_ms, 5),
+                "tensor": {"achieved_tflops": round(tflops, 2), "peak_tflops": tc_peak,
+                           "frac": round(tflops / tc_peak, 4)}}
+    graph = graph_batch(torch, step, flops_total, S, local)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if not args.no_cpu_baseline:
         gf, threads, med = cpu_baseline_run(A, Bh, steps=3, warmup=1)
         cpu = {"value": round(gf, 3), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"full {cfg_name} product, median of 3 (OpenMP static over rows, {med*1e3:.0f} ms each)"}
+               "sample": f"full c3 product in FP32, median of 3 (OpenMP static over rows, {med*1e3:.0f} ms each)"}
+    bplan.close()
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (reference generators, fixed seeds)", "config": config_dict("c3", A.nnz, world, True),
+        "e2e": None, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": K,
+        "parity": parity, "path": {"api": "spmm_bsr16_plan_execute (C ABI)", "kernel": kernel_name},
+        "graph_batch": graph,
+    }
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp16" if cfg_name == "c3" else "f32",
-            "data": "synthetic (reference generators, fixed seeds)",
-            "config": {"workload": CONFIGS[cfg_name], "config_id": cfg_name, "nnz": total_nnz, "N": N,
-                       "rows": A.rows, "cols": A.cols, "parallelism": f"row-split x{world} (nnz-balanced)",
-                       "kernel": kernel_name,
-                       "l2": "inputs larger than L2" if not small else "L2 flushed between steps",
-                       "b_broadcast_ms": round(bcast_ms, 4)},
-            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "gpu_launches": K * launches,
-            "graph_batch": graph,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+
+# ------------------------------------------------------------------------ reference arm
+
+
+def oracle_inputs(cfg: str, rows_prefix: int | None = None):
+    """Inputs made by the oracle's own generators (no product code): A as oracle.CSR, B float32.
+    For the uniform configs `rows_prefix` builds only the leading rows, which are the same rows
+    the full generator makes (the mt19937 Bernoulli scan runs row by row)."""
+    from oracle import oracle as O
+    from oracle import patterns as P
+
+    rows, cols, n = SHAPES[cfg]
+    if cfg in ("c1", "c5"):
+        d = 0.01 if cfg == "c1" else 0.001
+        A = O.gen_uniform_csr(rows if rows_prefix is None else rows_prefix, cols, d, 42)
+    else:
+        pat = {"c2": ("banded", {"bandwidth": 41}), "c3": ("block-diagonal", {"block": 128}),
+               "c4": ("power-law", {"mean_deg": 164.0, "alpha": 1.8})}[cfg]
+        rp, ci, v = P.make(pat[0], rows, cols, 42, **pat[1])
+        A = O.CSR(rows, cols, np.ascontiguousarray(rp, np.int32), np.ascontiguousarray(ci, np.int32),
+                  np.ascontiguousarray(v, np.float32))
+    return A, O.gen_dense(cols, n, 43)
+
+
+# nnz of every config's full matrix (the generators' outputs at seed 42), for the reference arm's
+# config dict when it builds only a sample of the rows.
+NNZ = {"c1": 167686, "c2": 678214, "c3": 1048576, "c4": 2686981, "c5": 17184511}
 
 
 def run_reference(args, rank: int, world: int):
-    """The reference semantics on the host cores; rank 0 only."""
+    """The reference semantics on the host cores; rank 0 only. Each step is the CSR x dense
+    product of a bounded sample of the workload (the leading rows, sized so that the whole run
+    stays within about a minute of CPU time); the rate (GFLOP/s) is the metric."""
     if rank != 0:
         return
-    A, Bh = build_inputs(args.config)
-    # Keep the whole run within ~150 s of CPU time: time one full product, and if the requested
-    # steps would exceed that, time each step on the leading rows only (same rate metric).
-    import spmm_b200 as S
+    from oracle import oracle as O
 
-    _, threads, one = cpu_baseline_run(A, Bh, steps=1, warmup=0)
-    sample = f"full {args.config} product per step (OpenMP static over rows)"
-    budget = 150.0
-    if (args.steps + args.warmup) * one > budget:
-        frac = max(budget / ((args.steps + args.warmup) * one), 1e-3)
-        rows = max(1, int(A.rows * frac))
-        A = S.row_slice(A, 0, rows)
-        sample = f"rows 0..{rows} of {args.config} ({100 * frac:.1f} % of the product) per step, OpenMP static"
+    cfg = args.config
+    rows, cols, n = SHAPES[cfg]
+    budget = 60.0
+    if cfg == "c5":
+        # Rate on a 4096-row prefix, then as many leading rows as the budget allows.
+        A, Bh = oracle_inputs(cfg, 4096)
+        _, threads, one = cpu_baseline_run(A, Bh, steps=1, warmup=1)
+        want = int(4096 * budget / ((args.steps + args.warmup) * max(one, 1e-6)))
+        take = max(1024, min(rows, want))
+        if take != 4096:
+            A = oracle_inputs(cfg, take)[0]
+        full_nnz = None
+    else:
+        A, Bh = oracle_inputs(cfg)
+        full_nnz = A.nnz
+        _, threads, one = cpu_baseline_run(A, Bh, steps=1, warmup=0)
+        take = rows
+        if (args.steps + args.warmup) * one > budget:
+            take = max(1, int(rows * budget / ((args.steps + args.warmup) * one)))
+            A = O.row_slice(A, 0, take)
+    sample = (f"rows 0..{take} of {cfg} ({100.0 * take / rows:.1f} % of the product) per step"
+              if take < rows else f"full {cfg} product per step")
+    sample += ", OpenMP static over rows; inputs from the oracle's generators"
     gf, threads, med = cpu_baseline_run(A, Bh, steps=args.steps, warmup=args.warmup)
+    nnz = full_nnz if full_nnz is not None else NNZ[cfg]
     line = {
         "metric": METRIC, "value": round(gf, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference generators, fixed seeds)",
-        "config": {"workload": CONFIGS[args.config], "config_id": args.config, "nnz": A.nnz, "N": Bh.shape[1]},
+        "vs_baseline": None, "dtype": "fp16" if cfg == "c3" else "f32",
+        "data": "synthetic (reference generators, fixed seeds)",
+        "config": config_dict(cfg, nnz, world, cfg != "c5"),
         "impl": "reference",
         "cpu_baseline": {"value": round(gf, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(gf, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

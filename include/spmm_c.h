@@ -227,7 +227,10 @@ int spmm_csr_f32_chunk(const spmm_csr_view* A, int32_t N, int32_t algo,
  * share the array, so calls that overlap on the GPU race; the counters that must start at
  * zero are cleared on `stream` before each launch. Bad indices are replaced by a safe one but
  * not reported (spmm_device_error does not see this path): validate A beforehand. Same
- * results as spmm_csr_f32 with the same algo, bit for bit. */
+ * results as spmm_csr_f32 with the same algo, bit for bit. Arguments are checked as
+ * spmm_csr_f32 checks them (SPMM_ERR_INVALID_ARG / SPMM_ERR_MISALIGNED) before the size check
+ * and before anything is queued. The array's address is looked up once per device and kept:
+ * do not call this entry point after cudaDeviceReset in the same process. */
 int spmm_csr_f32_noalloc(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
                          void* stream);
 
@@ -339,6 +342,77 @@ int spmm_gpu_count(void);
 int spmm_multigpu_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
                       int32_t num_gpus, int32_t warmup, int32_t iters, float* time_ms,
                       int32_t* used_gpus, int32_t* rows_out, int32_t* nnz_out, float* bcast_ms);
+
+/* ---------------------------------------------------------------- multi-GPU, one process per GPU
+ *
+ * The same row split for programs that run one process (or one long-lived host thread) per
+ * GPU, as torchrun and MPI jobs do. Every rank holds the whole host A and B and receives its
+ * own rows of C; the ranks exchange B over NVLink through an NCCL communicator, so B crosses
+ * the host links once in total instead of once per GPU. (reference: the per-GPU worker of
+ * src/spmm_multigpu.cu:66-109, which spmm_multigpu_run above runs as threads of one call) */
+
+#define SPMM_COMM_ID_BYTES 128
+typedef struct spmm_comm spmm_comm;
+
+/* A new communicator id (the bytes of an ncclUniqueId). Make it on one rank and hand the same
+ * bytes to every rank over any host channel (a TCP store, MPI, a shared file). */
+int spmm_comm_unique_id(uint8_t id[SPMM_COMM_ID_BYTES]);
+
+/* Join communicator `id` as `rank` of `world`, on the current device. Every rank calls it; it
+ * returns once all have joined, or SPMM_ERR_TIMEOUT after timeout_ms (<= 0: 300 s) when a rank
+ * never joins (the half-made communicator is then aborted). The same timeout bounds every
+ * later host wait on this communicator; a communicator that timed out is aborted and every
+ * further call on it returns SPMM_ERR_NCCL. */
+int spmm_comm_init(const uint8_t id[SPMM_COMM_ID_BYTES], int32_t world, int32_t rank, int32_t timeout_ms,
+                   spmm_comm** out);
+
+/* Wrap an NCCL communicator the caller already owns (an ncclComm_t passed as void*); its size,
+ * rank and device are read from it. spmm_comm_destroy then frees the wrapper only. */
+int spmm_comm_wrap(void* nccl_comm, int32_t timeout_ms, spmm_comm** out);
+int spmm_comm_info(const spmm_comm* comm, int32_t* world, int32_t* rank, int32_t* device);
+void spmm_comm_destroy(spmm_comm* comm);
+
+/* This rank's share of C = A * B under the reference's row split: rows [bounds[rank],
+ * bounds[rank + 1]) of spmm_nnz_balanced_bounds(A, world) (reference:
+ * src/spmm_multigpu.cu:26-40, 60-64). hA is the WHOLE host matrix, the same on every rank;
+ * comm = NULL is a world of one on the current device (no NCCL). Allocates the rank's device
+ * buffers (its rows of A, all of B, its rows of C), copies its rows of A once and inspects
+ * them (spmm_csr_plan_create). Local: no collective. Synchronises `stream`. */
+typedef struct spmm_rank_plan spmm_rank_plan;
+int spmm_rank_plan_create(spmm_comm* comm, const spmm_csr_view* hA, int32_t N, void* stream, spmm_rank_plan** out);
+
+/* The rank's rows [row_begin, row_end) and nonzeros; the rows of B it copies from the host
+ * itself, [b_row_begin, b_row_end) (B's rows in `world` shares of K * r / world); the CSR
+ * algorithm its plan picked and the kernel launches one spmm_rank_execute makes. Any pointer
+ * may be NULL. */
+int spmm_rank_plan_info(const spmm_rank_plan* plan, int32_t* row_begin, int32_t* row_end, int32_t* nnz,
+                        int32_t* b_row_begin, int32_t* b_row_end, int32_t* algo, int32_t* launches);
+
+/* One end-to-end multiply on host buffers; collective (every rank calls it, in the same order):
+ * the rank's rows of A and its share of B's rows go host -> device; the ranks all-gather B over
+ * NVLink (NCCL; ncclAllGather for equal shares, grouped send/recv otherwise); the kernels run on
+ * the rank's rows; its rows of C come back into hC_rows ((row_end - row_begin) x N row-major: a
+ * caller that holds the whole M x N C passes C + row_begin * N). hA must be the matrix the plan
+ * was made for: its values may change between calls, its structure may not (a row_ptr that
+ * differs at the rank's boundaries is refused). hB is the whole K x N B.
+ * Pipelined (one-warp-per-row plans): the all-gather overlaps the copy of A's rows, each of 8
+ * nnz-balanced row groups is launched once its rows have landed, and each group's rows of C go
+ * back while later groups compute. Bit-identical to spmm_rank_execute and to spmm_csr_f32 with
+ * the plan's algorithm on the rank's rows. Returns once hC_rows holds the result (the wait is
+ * bounded by the communicator's timeout). Pinned host buffers make the copies asynchronous. */
+int spmm_rank_run(spmm_rank_plan* plan, const spmm_csr_view* hA, const float* hB, float* hC_rows, void* stream);
+
+/* The kernels alone, on the device-resident operands the last spmm_rank_run left behind (the
+ * rank's rows of A and the gathered B), into the plan's device C. Asynchronous, not collective. */
+int spmm_rank_execute(spmm_rank_plan* plan, void* stream);
+
+/* The all-gather of B alone (device to device over NVLink, from the shares already on every
+ * rank's device). Collective, asynchronous on `stream`. */
+int spmm_rank_gather_b(spmm_rank_plan* plan, void* stream);
+
+/* The plan's device buffers: B (K x N, gathered) and the rank's rows of C. */
+int spmm_rank_plan_buffers(const spmm_rank_plan* plan, float** dB, float** dC);
+void spmm_rank_plan_destroy(spmm_rank_plan* plan);
 
 /* Managed-memory single-GPU path: A, B, C in cudaMallocManaged memory, prefetched to the
  * current device. *ms = median kernel time.

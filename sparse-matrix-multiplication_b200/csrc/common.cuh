@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <cstddef>
 #include <cstdint>
@@ -10,6 +11,16 @@
 #include "spmm_c.h"
 
 namespace spmm_b200 {
+
+// A named NVTX range over a host-side phase (copy issue, collective, launches), so that an
+// nsys or ncu timeline of the host-buffer and multi-GPU paths splits into its phases. NVTX v3
+// is header-only: without a profiler attached the push/pop calls return at once.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // Return SPMM_ERR_CUDA from the enclosing function when a runtime call fails.
 #define SPMM_CUDA_TRY(call)                                     \
@@ -80,6 +91,8 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
                    const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream, DeviceState* st,
                    bool ksplit_ready = false);
+// The argument checks csr_f32_launch makes first (view, pointers, alignment), on their own.
+int csr_f32_check_args(const spmm_csr_view* A, const float* B, const float* C, int32_t N);
 int csr_f32_workspace_bytes(const spmm_csr_view* A, int32_t N, int32_t algo, const spmm_csr_tuning* tune,
                             int sm_count, size_t* bytes);
 size_t csr_f32_counter_bytes(const spmm_csr_view* A, int32_t N, const spmm_csr_tuning* tune, int sm_count);

@@ -679,6 +679,10 @@ void launch(const Geometry& g, int algo, const CsrArgs& a, dim3 grid, cudaStream
 
 }  // namespace
 
+int csr_f32_check_args(const spmm_csr_view* A, const float* B, const float* C, int32_t N) {
+    return check_view(A, B, C, N);
+}
+
 // Shared by the C entry points below and by the allocation-free variant in noalloc.cu.
 int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
                    const spmm_csr_tuning* tune, void* ws, size_t ws_bytes, cudaStream_t stream,

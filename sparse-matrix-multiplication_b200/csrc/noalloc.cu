@@ -15,6 +15,9 @@
 // kernels overlap on the GPU (different streams, no ordering between them) race and give
 // wrong results. The arrival counters that must start at zero are cleared (cudaMemsetAsync
 // on the caller's stream) before every launch; the rest is overwritten before it is read.
+// The cached address belongs to the device's primary context: after cudaDeviceReset it no
+// longer names mapped memory, so this entry point must not be called again in a process that
+// has reset the device.
 
 #include <cuda_runtime.h>
 
@@ -58,7 +61,8 @@ using namespace spmm_b200;
 
 extern "C" int spmm_csr_f32_noalloc(const spmm_csr_view* A, const float* B, float* C, int32_t N, int32_t algo,
                                     void* stream) {
-    if (!A || N < 0) return SPMM_ERR_INVALID_ARG;
+    // The same argument checks as spmm_csr_f32, before anything is queued on the stream.
+    SPMM_TRY(csr_f32_check_args(A, B, C, N));
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) {
         cudaGetLastError();

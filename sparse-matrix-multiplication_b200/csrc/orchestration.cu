@@ -8,29 +8,18 @@
 
 #include <cuda_runtime.h>
 #include <dlfcn.h>
-#include <nccl.h>
 
 #include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
+#include "nccl_api.cuh"
 
 namespace spmm_b200 {
-
-// NCCL is resolved at run time (dlopen of libnccl.so.2) rather than linked: a process that
-// already holds an NCCL (e.g. the one PyTorch ships) keeps using it, and loading this library
-// never changes which NCCL the rest of the process sees.
-struct NcclApi {
-    ncclResult_t (*comm_init_all)(ncclComm_t*, int, const int*) = nullptr;
-    ncclResult_t (*group_start)() = nullptr;
-    ncclResult_t (*group_end)() = nullptr;
-    ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
-    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
-    bool ok = false;
-};
 
 const NcclApi& nccl() {
     static NcclApi api;
@@ -38,12 +27,26 @@ const NcclApi& nccl() {
     std::call_once(once, [] {
         void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
         if (!h) return;
-        api.comm_init_all = reinterpret_cast<decltype(api.comm_init_all)>(dlsym(h, "ncclCommInitAll"));
-        api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
-        api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
-        api.broadcast = reinterpret_cast<decltype(api.broadcast)>(dlsym(h, "ncclBroadcast"));
-        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        auto sym = [h](auto& fn, const char* name) { fn = reinterpret_cast<std::decay_t<decltype(fn)>>(dlsym(h, name)); };
+        sym(api.comm_init_all, "ncclCommInitAll");
+        sym(api.get_unique_id, "ncclGetUniqueId");
+        sym(api.comm_init_rank_config, "ncclCommInitRankConfig");
+        sym(api.comm_get_async_error, "ncclCommGetAsyncError");
+        sym(api.comm_count, "ncclCommCount");
+        sym(api.comm_user_rank, "ncclCommUserRank");
+        sym(api.comm_cu_device, "ncclCommCuDevice");
+        sym(api.comm_abort, "ncclCommAbort");
+        sym(api.comm_destroy, "ncclCommDestroy");
+        sym(api.group_start, "ncclGroupStart");
+        sym(api.group_end, "ncclGroupEnd");
+        sym(api.broadcast, "ncclBroadcast");
+        sym(api.all_gather, "ncclAllGather");
+        sym(api.send, "ncclSend");
+        sym(api.recv, "ncclRecv");
         api.ok = api.comm_init_all && api.group_start && api.group_end && api.broadcast && api.comm_destroy;
+        api.ranks_ok = api.ok && api.get_unique_id && api.comm_init_rank_config && api.comm_get_async_error &&
+                       api.comm_count && api.comm_user_rank && api.comm_cu_device && api.comm_abort &&
+                       api.all_gather && api.send && api.recv;
     });
     return api;
 }

@@ -41,6 +41,9 @@ EXPORTS = [
     "spmm_csr_f32_noalloc", "spmm_csr_to_bsr16_device_count", "spmm_csr_to_bsr16_device_fill",
     "spmm_csr_plan_create", "spmm_csr_plan_execute", "spmm_csr_plan_info", "spmm_csr_plan_destroy",
     "spmm_csr_plan_k_phases",
+    "spmm_comm_unique_id", "spmm_comm_init", "spmm_comm_wrap", "spmm_comm_info", "spmm_comm_destroy",
+    "spmm_rank_plan_create", "spmm_rank_plan_info", "spmm_rank_run", "spmm_rank_execute", "spmm_rank_gather_b",
+    "spmm_rank_plan_buffers", "spmm_rank_plan_destroy",
 ]
 
 
@@ -151,6 +154,19 @@ def lib() -> C.CDLL:
         "spmm_csr_plan_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_size_t)]),
         "spmm_csr_plan_k_phases": (C.c_int, [vp, C.POINTER(i32)]),
         "spmm_csr_plan_destroy": (None, [vp]),
+        "spmm_comm_unique_id": (C.c_int, [vp]),
+        "spmm_comm_init": (C.c_int, [vp, i32, i32, i32, C.POINTER(vp)]),
+        "spmm_comm_wrap": (C.c_int, [vp, i32, C.POINTER(vp)]),
+        "spmm_comm_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]),
+        "spmm_comm_destroy": (None, [vp]),
+        "spmm_rank_plan_create": (C.c_int, [vp, C.POINTER(CsrView), i32, vp, C.POINTER(vp)]),
+        "spmm_rank_plan_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32),
+                                          C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]),
+        "spmm_rank_run": (C.c_int, [vp, C.POINTER(CsrView), vp, vp, vp]),
+        "spmm_rank_execute": (C.c_int, [vp, vp]),
+        "spmm_rank_gather_b": (C.c_int, [vp, vp]),
+        "spmm_rank_plan_buffers": (C.c_int, [vp, C.POINTER(vp), C.POINTER(vp)]),
+        "spmm_rank_plan_destroy": (None, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -511,3 +527,96 @@ def unified_run_ex(A: HostCSR, B: np.ndarray, Cout: np.ndarray, N: int, device_b
     check(lib().spmm_unified_run_ex(C.byref(v), ptr(B), ptr(Cout), N, device_budget, warmup, iters, C.byref(ms),
                                     C.byref(ph)), "spmm_unified_run_ex")
     return float(ms.value), int(ph.value)
+
+
+# ------------------------------------------------------------------ multi-GPU, one process per GPU
+
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    """A fresh communicator id (spmm_comm_unique_id): make it on one rank, send the bytes to all."""
+    buf = (C.c_uint8 * COMM_ID_BYTES)()
+    check(lib().spmm_comm_unique_id(buf), "spmm_comm_unique_id")
+    return bytes(buf)
+
+
+class RankComm:
+    """spmm_comm_*: this process's member of an NCCL communicator over `world` ranks (one GPU each;
+    the current device is this rank's)."""
+
+    def __init__(self, comm_id: bytes, world: int, rank: int, timeout_ms: int = 0):
+        if len(comm_id) != COMM_ID_BYTES:
+            raise ValueError("communicator id must be 128 bytes")
+        buf = (C.c_uint8 * COMM_ID_BYTES).from_buffer_copy(comm_id)
+        h = C.c_void_p()
+        check(lib().spmm_comm_init(buf, world, rank, timeout_ms, C.byref(h)), "spmm_comm_init")
+        self._h = h
+        w, r, d = C.c_int32(), C.c_int32(), C.c_int32()
+        lib().spmm_comm_info(h, C.byref(w), C.byref(r), C.byref(d))
+        self.world, self.rank, self.device = int(w.value), int(r.value), int(d.value)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self) -> None:
+        if self._h:
+            lib().spmm_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+class RankPlan:
+    """spmm_rank_plan_*: this rank's share of C = A @ B under the reference's nnz-balanced row split.
+
+    A is the whole host CSR (the same on every rank); comm None is a world of one. run() is the
+    end-to-end multiply from host buffers (collective), execute() the kernels alone on the
+    device-resident operands the last run() left."""
+
+    def __init__(self, comm: RankComm | None, A: HostCSR, N: int, stream=None):
+        self._comm = comm
+        self._A = A
+        self.N = N
+        v = A.view()
+        h = C.c_void_p()
+        check(lib().spmm_rank_plan_create(comm.handle if comm else None, C.byref(v), N, stream_ptr(stream),
+                                          C.byref(h)), "spmm_rank_plan_create")
+        self._h = h
+        vals = [C.c_int32() for _ in range(7)]
+        check(lib().spmm_rank_plan_info(h, *[C.byref(x) for x in vals]), "spmm_rank_plan_info")
+        (self.row_begin, self.row_end, self.nnz, self.b_row_begin, self.b_row_end, self.algo,
+         self.launches) = (int(x.value) for x in vals)
+        dB, dC = C.c_void_p(), C.c_void_p()
+        check(lib().spmm_rank_plan_buffers(h, C.byref(dB), C.byref(dC)), "spmm_rank_plan_buffers")
+        self.d_B, self.d_C = int(dB.value or 0), int(dC.value or 0)
+
+    @property
+    def rows(self) -> int:
+        return self.row_end - self.row_begin
+
+    def run(self, A: HostCSR, B: np.ndarray, C_rows: np.ndarray, stream=None) -> None:
+        v = A.view()
+        check(lib().spmm_rank_run(self._h, C.byref(v), ptr(B), ptr(C_rows), stream_ptr(stream)), "spmm_rank_run")
+
+    def execute(self, stream=None) -> None:
+        check(lib().spmm_rank_execute(self._h, stream_ptr(stream)), "spmm_rank_execute")
+
+    def gather_b(self, stream=None) -> None:
+        check(lib().spmm_rank_gather_b(self._h, stream_ptr(stream)), "spmm_rank_gather_b")
+
+    def close(self) -> None:
+        if self._h:
+            lib().spmm_rank_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass

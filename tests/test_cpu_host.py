@@ -275,6 +275,13 @@ def test_device_entry_points_fail_loudly_without_gpu():
         S.csr_f32_host(A, B, C, 4)
     assert e.value.status == -6  # SPMM_ERR_UNSUPPORTED, never a silent CPU fallback
     assert S.gpu_count() == 0
+    # The per-rank multi-GPU path refuses as well, with or without a communicator.
+    with pytest.raises(S.SpmmError) as e:
+        S.RankPlan(None, A, 4)
+    assert e.value.status == -6
+    with pytest.raises(S.SpmmError) as e:
+        S.RankComm(bytes(S.COMM_ID_BYTES), 2, 0, timeout_ms=1000)
+    assert e.value.status == -6
 
 
 def test_status_strings():

@@ -70,3 +70,7 @@ def test_noalloc_refuses_requests_beyond_its_scratch(cuda):
     rc = _noalloc(view, dummy, dummy, 512, S.CSR_AUTO, torch.cuda.current_stream())
     assert rc == -10  # SPMM_ERR_TOO_LARGE
     assert _noalloc(view, dummy, dummy, -1, S.CSR_AUTO, None) == -1
+    # A null B (or C) is an invalid argument, reported before the size check and before
+    # anything is queued on the stream.
+    assert _noalloc(view, None, dummy, 512, S.CSR_AUTO, None) == -1
+    assert _noalloc(view, dummy, None, 512, S.CSR_AUTO, None) == -1
