@@ -34,9 +34,19 @@ def _cpu_has_v3() -> bool:
 def build() -> None:
     """Compile the oracle (and, when the reference checkout is present, oracle/_ref)."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
-    ref_src = Path(os.environ.get("SPMM_REF_SRC", "/root/reference/src"))
-    if ref_src.is_dir():
+    ref_src = ref_source()
+    if ref_src is not None:
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_SRC={ref_src}"], check=True)
+
+
+def ref_source() -> Path | None:
+    """The reference's src/ directory: $SPMM_REF_SRC, else the location the last `make ref`
+    recorded in oracle/_ref/REF_SRC; None when neither names an existing directory (the
+    reference is only present where the fixtures are made, never on the GPU box)."""
+    env = os.environ.get("SPMM_REF_SRC")
+    rec = HERE / "_ref" / "REF_SRC"
+    cand = env if env else (rec.read_text().strip() if rec.exists() else "")
+    return Path(cand) if cand and Path(cand).is_dir() else None
 
 
 _lib = None

@@ -10,7 +10,7 @@ Sources, none of which exist on the GPU box (the JSON is committed instead):
     scripts/roofline.py:59-154 (nnz per sweep cell), reports/tensor_core_wmma.md:43-56
     (BSR block counts), README.md:233 (4096^2 d=0.01 -> 167686).
 
-Usage:  python tests/golden/make_golden.py [--ref /root/reference]
+Usage:  python tests/golden/make_golden.py --ref <reference checkout>
 """
 from __future__ import annotations
 
@@ -86,7 +86,7 @@ def pattern_csr(gm, pattern, rows, cols, kw, seed=42):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--ref", type=Path, required=True, help="the reference checkout (its top directory)")
     args = ap.parse_args()
     gm = load_gen_matrices(args.ref)
     from oracle import oracle as O

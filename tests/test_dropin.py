@@ -14,10 +14,11 @@ import numpy as np
 import pytest
 
 import spmm_b200 as S
+from oracle import oracle as O
 
 REPO = Path(__file__).resolve().parent.parent
 DROP = REPO / "oracle" / "_ref" / "dropin"
-REF_SRC = Path(os.environ.get("SPMM_REF_SRC", "/root/reference/src"))
+REF_SRC = O.ref_source()  # $SPMM_REF_SRC, or where the last `make -C oracle ref` found the reference
 LINE = re.compile(r"(\w+)=([^\s]+)")
 
 
@@ -25,7 +26,7 @@ def parse(out: str, prefix: str) -> list[dict]:
     return [dict(LINE.findall(line)) for line in out.splitlines() if line.startswith(prefix)]
 
 
-@pytest.mark.skipif(not REF_SRC.is_dir(), reason="reference checkout not present")
+@pytest.mark.skipif(REF_SRC is None, reason="reference sources not found: set SPMM_REF_SRC=<reference>/src")
 def test_reference_drivers_compile_unchanged_against_our_headers():
     subprocess.run(["make", "-s", "-C", str(REPO / "oracle"), "dropin", f"REF_SRC={REF_SRC}"], check=True)
     for exe in ("spmm_bench", "spmm_run"):
