@@ -32,6 +32,11 @@ that rank runs at G GPUs), to profile a rank's launch with ncu on a single GPU.
 `--impl reference` times the reference's CSR x dense semantics on the host cores (the
 oracle's OpenMP port: the reference ships no CPU SpMM of its own) on rank 0 only, on inputs made
 by the oracle's own generators.
+
+`--impl reference-gpu` is a same-box comparison on one GPU: the reference's own CUDA kernels,
+compiled unchanged for sm_100a from its sources into oracle/_ref/libref.so (tiled_v3, the kernel
+its multi-GPU path runs, for the CSR configs; spmm_wmma for config 3), against this engine's
+kernels on the same inputs with the same CUDA events; both outputs are compared.
 """
 from __future__ import annotations
 
@@ -75,7 +80,7 @@ def parse():
     p.add_argument("--steps", type=int, default=None)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--config", default="c5", choices=sorted(CONFIGS))
-    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
     p.add_argument("--rank-slice", default=None, help="R/G: rank R's rows of a G-way split, alone on one GPU")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -335,6 +340,8 @@ def main():
 
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.impl == "reference-gpu":
+        return run_reference_gpu(args, rank, world)
 
     import torch
     import torch.distributed as dist
@@ -702,6 +709,107 @@ def run_reference(args, rank: int, world: int):
         "cpu_baseline": {"value": round(gf, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(gf, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_gpu(args, rank: int, world: int):
+    """Same-box GPU comparison (rank 0, one GPU): the reference's kernels recompiled for sm_100a
+    (oracle/_ref/libref.so, built from the reference's sources by oracle/Makefile) against this
+    engine's, on inputs from the oracle's generators, timed with the same CUDA events."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    cfg = args.config
+    rows, cols, n = SHAPES[cfg]
+    base = {"metric": METRIC, "unit": UNIT, "impl": "reference-gpu", "n_gpus": 1,
+            "config": config_dict(cfg, NNZ[cfg], 1, cfg != "c5")}
+    if not O.ref_available():
+        print(json.dumps({**base, "unavailable": "oracle/_ref/libref.so not built (make -C oracle ref)"}), flush=True)
+        return
+    import ctypes as C
+
+    import torch
+
+    import spmm_b200 as S
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    R = O.ref()
+    A, Bh = oracle_inputs(cfg)
+    N = Bh.shape[1]
+    flops = 2.0 * A.nnz * N
+    K = args.steps
+    to_dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)  # noqa: E731
+    rp, ci, va = to_dev(A.row_ptr), to_dev(A.col_idx), to_dev(A.values)
+    stream = torch.cuda.current_stream()  # the legacy default stream, where the reference launches
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(K):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / K
+
+    vp = C.c_void_p
+    if cfg == "c3":
+        Ab = O.bsr_from_csr(A)
+        B16 = O.to_half_bits(Bh)
+        brp, bci, bva = to_dev(Ab.row_ptr), to_dev(Ab.col_idx), to_dev(Ab.values.view(np.int16))
+        Bd16 = to_dev(B16.view(np.int16))
+        C_ref = torch.zeros((rows, N), dtype=torch.float32, device=dev)
+        C_our = torch.zeros((rows, N), dtype=torch.float32, device=dev)
+
+        def ref_step():
+            R.ref_spmm_wmma_device(rows, cols, Ab.block_rows, Ab.block_cols, Ab.num_blocks, A.nnz, vp(brp.data_ptr()),
+                                   vp(bci.data_ptr()), vp(bva.data_ptr()), vp(Bd16.data_ptr()), vp(C_ref.data_ptr()), N)
+
+        view = S.BsrView(rows, cols, Ab.block_rows, Ab.block_cols, Ab.num_blocks, A.nnz, S.ptr(brp), S.ptr(bci),
+                         S.ptr(bva), S.DTYPE_F16)
+        plan = S.BsrPlan(view, N, stream=stream)
+        ms_ref = timed(ref_step)
+        ms_our = timed(lambda: plan.execute(Bd16, C_our, stream))
+        ref64 = O.spmm_bsr_f64(Ab, B16, 0)
+        scale = max(float(np.abs(ref64).max()), 1e-30)
+        e_ref = float(np.abs(C_ref.cpu().numpy() - ref64).max()) / scale
+        e_our = float(np.abs(C_our.cpu().numpy() - ref64).max()) / scale
+        parity = {"max_err_over_max_ref": {"reference": e_ref, "ours": e_our}, "ok": e_our <= 1e-5,
+                  "oracle": "oracle.spmm_bsr_f64 on the same FP16 inputs"}
+        names = ("spmm_wmma (reference, nvcuda::wmma)", "bsr_tcgen05_kernel (planned)")
+        plan.close()
+    else:
+        Bd = to_dev(Bh)
+        C_ref = torch.zeros((rows, N), dtype=torch.float32, device=dev)
+
+        def ref_step():
+            R.ref_spmm_csr_device(5, rows, cols, A.nnz, vp(rp.data_ptr()), vp(ci.data_ptr()), vp(va.data_ptr()),
+                                  vp(Bd.data_ptr()), vp(C_ref.data_ptr()), N)
+
+        hA = S.HostCSR(rows, cols, A.row_ptr, A.col_idx, A.values)
+        plan = S.RankPlan(None, hA, N, stream)
+        hC = np.empty((rows, N), np.float32)
+        plan.run(hA, Bh, hC, stream)
+        ms_ref = timed(ref_step)
+        ms_our = timed(lambda: plan.execute(stream))
+        plan.run(hA, Bh, hC, stream)
+        got_ref = C_ref.cpu().numpy()
+        same = bool(np.array_equal(got_ref.view(np.uint32), hC.view(np.uint32)))
+        parity = {"bit_identical_to_reference_kernel": same, "ok": same or plan.algo == S.CSR_MERGE,
+                  "compare_vs_reference": list(O.compare(hC, got_ref))}
+        names = ("spmm_tiled_v3 (reference)",
+                 "csr_rowwarp_kernel" if plan.algo == S.CSR_ROWWARP else "csr_merge_kernel")
+        plan.close()
+    line = {**base, "value": round(flops / (ms_ref * 1e-3) / 1e9, 3), "ms_per_step": round(ms_ref, 5),
+            "steps": K, "warmup": args.warmup, "higher_is_better": True, "reference_kernel": names[0],
+            "ours": {"kernel": names[1], "ms_per_step": round(ms_our, 5),
+                     "value": round(flops / (ms_our * 1e-3) / 1e9, 3)},
+            "speedup_ours_over_reference": round(ms_ref / ms_our, 3), "parity": parity,
+            "data": "synthetic (the oracle's generators, fixed seeds)", "gpu": torch.cuda.get_device_name(0)}
     print(json.dumps(line), flush=True)
 
 

@@ -13,6 +13,24 @@ CSR/TC crossover in fill-in is what the hybrid threshold is set from.
 
 Times are CUDA-event medians of single launches with a 256 MiB L2 flush in between.
 
+    python sparse-matrix-multiplication_b200/sweep.py --pattern-sweep --out pattern_sweep.csv [--dry-run]
+
+runs the reference's own cross-pattern grid (scripts/run_pattern_sweep.py: uniform d=0.01,
+banded bandwidth 32, block-diagonal block 16, power-law mean degree 32 alpha 2.5; m = 1024, 4096,
+8192, 16384; N = 256; seed 42, the same generator call sequence) and writes the reference's tidy
+CSV, one row per (pattern, size, kernel) with exactly its columns
+(pattern,kernel,m,k,n,nnz,density,time_ms,gflops). Kernels: csr_rowwarp, csr_merge, bsr16_tc
+(tcgen05, FP16) and hybrid[<choice>] (the hybrid rule's pick at --threshold). --dry-run builds
+the matrices on the CPU and writes the rows without timings.
+
+    python sparse-matrix-multiplication_b200/sweep.py --roofline-from pattern_sweep.csv --out roofline.csv
+
+turns such a CSV into the reference's roofline table (scripts/roofline.py:177-212: compulsory
+DRAM bytes 8*nnz + 4(m+1) + 4*k*n + 4*m*n, AI, ceiling min(FP32 peak, AI * DRAM bandwidth), % of
+FP32 peak, % of the ceiling, effective DRAM bandwidth, bound, B_fits_L2) with B200 ceilings: the
+measured HBM bandwidth (MEASURED_PEAKS.json), the FP32 CUDA-core peak (148 SMs x 128 lanes x
+2 FLOP x the maximum SM clock) and the 126 MB L2. CPU only.
+
     python sparse-matrix-multiplication_b200/sweep.py --gather-footprints --out gather.csv
 
 instead measures the gather ceiling that bounds the FP32 CSR kernels: for B footprints from 8 MB
@@ -58,6 +76,147 @@ def cases(quick: bool):
     for blk in ((8, 16, 128) if quick else (4, 8, 12, 16, 32, 64, 128)):
         yield f"blockdiag_8192_b{blk}", lambda blk=blk: SP.host_csr(8192, 8192, SP.block_diagonal_arrays(8192, 8192, blk, 42))
     yield "powerlaw_16384", lambda: SP.host_csr(16384, 16384, SP.power_law_arrays(16384, 16384, 164.0, 1.8, 42))
+
+
+# The reference's cross-pattern grid (scripts/run_pattern_sweep.py:46-51 generator parameters,
+# :92-93 sizes, :94 N) and its CSV columns (:147); the roofline table's columns
+# (scripts/roofline.py:236-239).
+PATTERN_PARAMS = {"uniform": {"density": 0.01}, "banded": {"bandwidth": 32}, "block-diagonal": {"block": 16},
+                  "power-law": {"mean_deg": 32.0, "alpha": 2.5}}
+PATTERN_SIZES = (1024, 4096, 8192, 16384)
+PATTERN_SWEEP_COLUMNS = ["pattern", "kernel", "m", "k", "n", "nnz", "density", "time_ms", "gflops"]
+ROOFLINE_COLUMNS = ["kernel", "m", "density", "nnz", "gflops", "ai_flop_per_byte", "ceiling_gflops", "pct_fp32_peak",
+                    "pct_roofline", "eff_dram_bw_gbs", "pct_dram_bw", "bound", "B_fits_L2"]
+B200_SMS = 148
+B200_L2_BYTES = 126 * 1024 * 1024
+FP32_LANES_PER_SM = 128
+
+
+def pattern_matrix(pattern: str, m: int, seed: int = 42) -> S.HostCSR:
+    """An m x m matrix of one of the reference's sweep patterns (gen_matrices.py's call sequence)."""
+    kw = PATTERN_PARAMS[pattern]
+    if pattern == "uniform":
+        arrays = SP.uniform_mask_arrays(m, m, kw["density"], seed)
+    elif pattern == "banded":
+        arrays = SP.banded_arrays(m, m, kw["bandwidth"], seed)
+    elif pattern == "block-diagonal":
+        arrays = SP.block_diagonal_arrays(m, m, kw["block"], seed)
+    else:
+        arrays = SP.power_law_arrays(m, m, kw["mean_deg"], kw["alpha"], seed)
+    return SP.host_csr(m, m, arrays)
+
+
+def b200_ceilings() -> tuple[float, float, int]:
+    """(FP32 CUDA-core peak GFLOP/s, DRAM GB/s, L2 bytes): the peak from the SM count and the
+    maximum SM clock, the bandwidth measured by the driver (MEASURED_PEAKS.json)."""
+    mhz = 1965.0
+    try:
+        mhz = float(json.loads((HERE.parent / "MEASURED_PEAKS.json").read_text()).get("sm_max_mhz", mhz))
+    except (OSError, ValueError):
+        pass
+    return B200_SMS * FP32_LANES_PER_SM * 2 * mhz / 1e3, peak_hbm_gbs(), B200_L2_BYTES
+
+
+def roofline_rows(rows, fp32_gflops: float, dram_gbs: float, l2_bytes: int) -> list[dict]:
+    """The reference's roofline analysis (scripts/roofline.py:177-212) of sweep rows with the
+    given ceilings: compulsory bytes, AI, min(peak, AI * bandwidth), the percentages, the bound."""
+    ridge = fp32_gflops / dram_gbs
+    out = []
+    for r in rows:
+        m, k, n, nnz = int(r["m"]), int(r["k"]), int(r["n"]), int(r["nnz"])
+        t = float(r["time_ms"])
+        gflops = float(r["gflops"])
+        flops = 2.0 * nnz * n
+        dram = 8 * nnz + 4 * (m + 1) + 4 * k * n + 4 * m * n
+        ai = flops / dram
+        ceiling = min(fp32_gflops, ai * dram_gbs)
+        eff = dram / (t * 1e6)
+        out.append({"kernel": r["kernel"], "m": m, "density": float(r.get("density") or nnz / (m * k)), "nnz": nnz,
+                    "gflops": gflops, "ai_flop_per_byte": ai, "ceiling_gflops": ceiling,
+                    "pct_fp32_peak": 100.0 * gflops / fp32_gflops, "pct_roofline": 100.0 * gflops / ceiling,
+                    "eff_dram_bw_gbs": eff, "pct_dram_bw": 100.0 * eff / dram_gbs,
+                    "bound": "compute/L2" if ai > ridge else "memory", "B_fits_L2": 4 * k * n <= l2_bytes,
+                    "pattern": r.get("pattern", "")})
+    return out
+
+
+def roofline_from(args) -> None:
+    with open(args.roofline_from, newline="") as fh:
+        # Timed rows only (a dry run leaves time_ms and gflops empty).
+        rows = [r for r in csv.DictReader(fh) if r.get("time_ms") and r.get("gflops") and float(r["time_ms"]) > 0]
+    fp32, dram, l2 = b200_ceilings()
+    res = roofline_rows(rows, fp32, dram, l2)
+    with open(args.out, "w", newline="") as fh:
+        w = csv.DictWriter(fh, fieldnames=ROOFLINE_COLUMNS, extrasaction="ignore")
+        w.writeheader()
+        w.writerows(res)
+    print(f"B200 ceilings: FP32 {fp32:.0f} GFLOP/s | DRAM {dram:.0f} GB/s | ridge {fp32 / dram:.1f} FLOP/byte | "
+          f"L2 {l2 // (1024 * 1024)} MB")
+    for r in res:
+        print(f"{r['pattern']:>15} {r['kernel']:>14} m={r['m']:<6d} AI {r['ai_flop_per_byte']:6.1f} "
+              f"{r['gflops']:9.1f} GFLOP/s  {r['pct_roofline']:5.1f}% of roof  {r['pct_dram_bw']:5.1f}% of DRAM")
+
+
+def pattern_sweep(args) -> None:
+    """The reference's cross-pattern grid on this engine (see the module docstring)."""
+    rows = []
+    timer = None
+    if not args.dry_run:
+        import torch
+
+        torch.cuda.set_device(0)
+        dev = torch.device("cuda", 0)
+        stream = torch.cuda.current_stream()
+        flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+        timer = (torch, dev, stream, flush)
+    N = args.n
+    sizes = [m for m in PATTERN_SIZES if m <= args.max_size]
+    with open(args.out, "w", newline="") as fh:
+        w = csv.DictWriter(fh, fieldnames=PATTERN_SWEEP_COLUMNS, extrasaction="ignore")
+        w.writeheader()
+        for pattern in args.patterns or list(PATTERN_PARAMS):
+            for m in sizes:
+                A = pattern_matrix(pattern, m)
+                base = {"pattern": pattern, "m": m, "k": m, "n": N, "nnz": A.nnz, "density": A.nnz / (m * m)}
+                choice = S.hybrid_choose(A, N, args.threshold)["backend_name"]
+                if timer is None:
+                    times = {"csr_rowwarp": None, "csr_merge": None, "bsr16_tc": None}
+                else:
+                    times = time_pattern_case(timer, A, N, args.reps)
+                times[f"hybrid[{choice}]"] = (times["bsr16_tc"] if choice == "wmma"
+                                              else min(times["csr_rowwarp"], times["csr_merge"])
+                                              if times["csr_rowwarp"] is not None else None)
+                for kernel, t in times.items():
+                    row = {**base, "kernel": kernel, "time_ms": "" if t is None else round(t, 5),
+                           "gflops": "" if t is None else round(2.0 * A.nnz * N / (t * 1e-3) / 1e9, 2)}
+                    rows.append(row)
+                    w.writerow(row)
+                fh.flush()
+                print(json.dumps({k: base[k] for k in ("pattern", "m", "nnz")} | {"times_ms": times}), flush=True)
+    if timer is not None:
+        code, detail = S.device_error(0)
+        if code:
+            raise SystemExit(f"device error {code} ({detail})")
+
+
+def time_pattern_case(timer, A: S.HostCSR, N: int, reps: int) -> dict:
+    torch, dev, stream, flush = timer
+    M, K = A.rows, A.cols
+    Bh = S.generate_dense(K, N, 43)
+    rp, ci, v = (torch.from_numpy(x).to(dev) for x in (A.row_ptr, A.col_idx, A.values))
+    B = torch.from_numpy(Bh).to(dev)
+    C = torch.empty((M, N), device=dev)
+    view = S.device_view(M, K, rp, ci, v)
+    out = {"csr_rowwarp": time_ms(torch, lambda: S.csr_f32(view, B, C, N, S.CSR_ROWWARP, stream), reps, flush),
+           "csr_merge": time_ms(torch, lambda: S.csr_f32(view, B, C, N, S.CSR_MERGE, stream), reps, flush)}
+    bview, keep = S.csr_to_bsr16_device(view, S.DTYPE_F16, stream)
+    B16 = torch.empty((K, N), dtype=torch.float16, device=dev)
+    S.convert_f32(B, B16, K * N, S.DTYPE_F16, stream)
+    bplan = S.BsrPlan(bview, N, stream=stream)
+    out["bsr16_tc"] = time_ms(torch, lambda: bplan.execute(B16, C, stream), reps, flush)
+    bplan.close()
+    del keep
+    return out
 
 
 def time_ms(torch, fn, reps: int, flush) -> float:
@@ -157,9 +316,20 @@ def main():
     ap.add_argument("--quick", action="store_true")
     ap.add_argument("--gather-footprints", action="store_true",
                     help="probe vs CSR kernel gather rate over B footprints (see above)")
+    ap.add_argument("--pattern-sweep", action="store_true", help="the reference's cross-pattern grid (see above)")
+    ap.add_argument("--patterns", nargs="+", default=None, choices=sorted(PATTERN_PARAMS))
+    ap.add_argument("--max-size", type=int, default=max(PATTERN_SIZES), help="largest m of the pattern grid")
+    ap.add_argument("--dry-run", action="store_true", help="pattern sweep: build the matrices, no GPU, no timings")
+    ap.add_argument("--roofline-from", type=Path, default=None, help="pattern-sweep CSV to analyse (CPU only)")
     args = ap.parse_args()
     if args.gather_footprints:
         gather_footprints(args)
+        return
+    if args.roofline_from is not None:
+        roofline_from(args)
+        return
+    if args.pattern_sweep:
+        pattern_sweep(args)
         return
 
     import torch

@@ -77,3 +77,31 @@ def test_spmm_run_modes_pass(cuda, tmp_path):
     plan = parse(out, "plan ")[0]
     assert plan["backend"] == "wmma" and abs(float(plan["fill_in"]) - 1.35) < 0.01
     assert "[PASS]" in out
+
+
+@pytest.mark.gpu
+@needs_bins
+def test_spmm_run_threshold_flag_selects_b200_routing(cuda, tmp_path):
+    """The unchanged spmm_run always passes its own --threshold (default 2.0, the T4 cut-off,
+    spmm_run.cu:35,189) to hybrid_choose, so the library's B200 default (6.0) never reaches it;
+    B200 routing through that driver needs --threshold 6. Banded bandwidth 6 has fill-in 3.69:
+    the T4 cut-off sends it to the CUDA cores, the B200 one to the tensor cores."""
+    import spmm_patterns as SP
+
+    A = SP.host_csr(8192, 8192, SP.banded_arrays(8192, 8192, 6, 42))
+    f = tmp_path / "banded_bw6.bin"
+    S.write_binary(A, f)
+    base = [str(DROP / "spmm_run"), "--bin", str(f), "--n", "128", "--iters", "3"]
+    plan = parse(run(base), "plan ")[0]
+    assert plan["backend"] == "csr" and float(plan["threshold"]) == 2.0
+    out = run(base + ["--threshold", "6"])
+    plan = parse(out, "plan ")[0]
+    assert plan["backend"] == "wmma" and float(plan["threshold"]) == 6.0
+    assert abs(float(plan["fill_in"]) - 3.69) < 0.01
+    assert "[PASS]" in out
+    # Config 2 (banded 41, fill-in 1.35) stays on the tensor cores with the B200 cut-off.
+    A2 = SP.host_csr(8192, 8192, SP.banded_arrays(8192, 8192, 41, 42))
+    f2 = tmp_path / "banded_bw41.bin"
+    S.write_binary(A2, f2)
+    out = run([str(DROP / "spmm_run"), "--bin", str(f2), "--n", "128", "--iters", "3", "--threshold", "6"])
+    assert parse(out, "plan ")[0]["backend"] == "wmma" and "[PASS]" in out
