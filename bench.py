@@ -427,7 +427,7 @@ def run_csr(args, torch, dist, R: Ranks, rank: int, world: int, local: int) -> d
     clocks = Clocks(local, enabled=not args.no_clocks)
     clocks.start()
     K = args.steps
-    ms_rank, avg_launch_ms = time_steps(torch, step, K, stream, flush, R)
+    ms_rank, avg_step_ms = time_steps(torch, step, K, stream, flush, R)
     clk = clocks.stop()
     ms_step = R.max(ms_rank)
     code, detail = S.device_error(local)
@@ -462,24 +462,26 @@ def run_csr(args, torch, dist, R: Ranks, rank: int, world: int, local: int) -> d
                          if plan.algo == S.CSR_ROWWARP else "oracle.spmm_csr_f32_split (merge-path cut), all rows"),
               "source": "C rows of the last end-to-end step (host)"}
 
-    # ---- roofline of the dominant kernel (per launch, this rank; rank 0 reports)
+    # ---- roofline of the dominant kernel, per step (one pass over the rank's rows: `launches`
+    # launches of it when the plan cuts A's columns into phases), this rank; rank 0 reports
     alg_bytes = 8 * plan.nnz + 4 * (rows_r + 1) + 4 * A.cols * N + 4 * rows_r * N
     launches = max(plan.launches, 1)
-    achieved = alg_bytes / (avg_launch_ms * 1e-3) / 1e9
+    achieved = alg_bytes / (avg_step_ms * 1e-3) / 1e9
     gpus_key = args.rank_slice[1] if args.rank_slice is not None else world
     traffic = None
     prof = REPO / "profiles" / f"{kernel_name}_config{cfg_name[1:]}.md"
     if prof.exists():
-        key = f"dram_bytes_per_launch_gpus{gpus_key}:"
+        key = f"dram_bytes_per_step_gpus{gpus_key}:"
         for ln in prof.read_text().splitlines():
             if ln.startswith(key):
                 traffic = int(ln.split(":", 1)[1].strip())
     roofline = {"bound": "hbm", "kernel": kernel_name, "achieved": round(achieved, 1), "peak": hbm_peak,
                 "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
-                "alg_bytes_per_launch": int(alg_bytes), "avg_launch_ms": round(avg_launch_ms, 5)}
-    gathered = 4.0 * plan.nnz * N  # B-row bytes the gather moves through L2 per launch
-    gather_gbs = gathered / (avg_launch_ms * 1e-3) / 1e9
+                "alg_bytes_per_step": int(alg_bytes), "avg_step_ms": round(avg_step_ms, 5),
+                "launches_per_step": launches, "per": "step (one pass over the rank's rows)"}
+    gathered = 4.0 * plan.nnz * N  # B-row bytes the gather moves through L2 per step
+    gather_gbs = gathered / (avg_step_ms * 1e-3) / 1e9
     roofline["l2_gather_gbs"] = round(gather_gbs, 1)
     # The ceiling that bounds a gather of whole B rows: a load-only probe that pulls random
     # 1 KB rows into the SMs from an L2-resident 32 MB part of B, and the same probe over B's

@@ -238,10 +238,12 @@ int spmm_csr_f32_noalloc(const spmm_csr_view* A, const float* B, float* C, int32
  * launchers re-derive everything per call). spmm_csr_plan_create reads A's device row_ptr
  * once (one small kernel, synchronises `stream`) and picks the work distribution:
  * SPMM_CSR_ROWWARP when the longest row is at most max(4 * (M + nnz) / resident warps, 256),
- * else SPMM_CSR_MERGE. With ROWWARP and tune->k_phases == 0 it also picks column phases:
- * more than one only when B (cols * N * 4 bytes) exceeds 1.2x the L2 and the launch gathers
- * at least 12 GB (nnz * N * 4), then about one phase per half L2 of B; it computes the phase
- * split positions once (one pass over col_idx). It allocates the plan's workspace.
+ * else SPMM_CSR_MERGE. With ROWWARP and tune->k_phases == 0 it also picks column phases by the
+ * size of B (cols * N * 4 bytes) against the L2 and the bytes a launch gathers (nnz * N * 4):
+ * 3 phases when B is 0.8x to 1.2x the L2 and the launch gathers at least 4 GB; about one phase
+ * per half L2 of B when B exceeds 1.2x the L2 and the launch gathers at least 12 GB; else one.
+ * It computes the phase split positions once (one pass over col_idx) and allocates the plan's
+ * workspace.
  * spmm_csr_plan_execute launches only (no allocation, asynchronous); A's arrays must stay
  * valid and unchanged. Results equal spmm_csr_f32 with the chosen algo bit for bit. */
 typedef struct spmm_csr_plan spmm_csr_plan;

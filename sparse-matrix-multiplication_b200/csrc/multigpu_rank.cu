@@ -457,8 +457,11 @@ int spmm_rank_plan_create(spmm_comm* comm, const spmm_csr_view* hA, int32_t N, v
     spmm_csr_plan_info(p->cplan, &p->algo, nullptr, nullptr);
     spmm_csr_plan_k_phases(p->cplan, &p->k_phases);
     // Row groups: ROWWARP computes every row on its own, so any grouping of the rows into
-    // launches gives the same bits; other plans run as one launch once all rows have landed.
-    p->pipelined = p->algo == SPMM_CSR_ROWWARP && p->k_phases == 1 && rows >= 2 * kRankGroups && N > 0;
+    // launches gives the same bits, with or without the plan's column phases (each element's
+    // chain is the same however its positions are cut); the pipelined run launches each group
+    // unphased, since its kernels hide behind the copies. Merge plans run as one launch once
+    // all rows have landed.
+    p->pipelined = p->algo == SPMM_CSR_ROWWARP && rows >= 2 * kRankGroups && N > 0;
     const int G = p->pipelined ? kRankGroups : 1;
     p->groups.resize(G + 1);
     if (p->pipelined) {

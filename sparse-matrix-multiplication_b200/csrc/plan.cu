@@ -43,17 +43,23 @@ __global__ void max_row_kernel(const int* __restrict__ row_ptr, int M, int* out)
 
 // Column phases for ROWWARP. A random-row gather runs at the L2 rate (about 19-20 TB/s on
 // B200) while B fits in about 80 % of the L2, and falls towards the HBM rate beyond it
-// (14 TB/s at 128 MiB, 8 TB/s at 512 MiB). Phases of about half the L2 each bring B back
-// into range at the price of re-reading and re-writing C per phase and one launch per
-// phase, which only pays off on large launches. Measured on B200 (131072 rows x 131 nnz,
-// N = 256): 160 MiB of B 3 phases -4 %, 256 MiB 4 phases -13 %, 512 MiB 8 phases -38 %
-// of the time; at 128 MiB (config 5) 2 phases tie with one, and launches of 65536 or 16384
-// rows with 128 MiB of B got 3 % and 7 % slower. So: B above 1.2x the L2 and >= 12 GB gathered.
+// (14 TB/s at 128 MiB, 8 TB/s at 512 MiB). Phases bring B's footprint back into range at the
+// price of re-reading and re-writing C per phase and one launch per phase, which only pays off
+// on large launches. Measured on B200 (131072 rows x 131 nnz, N = 256), two regimes:
+//   * B from 0.8x to 1.2x the L2 (config 5: 128 MiB, 1.06x): 400 back-to-back launches, where
+//     one phase's 4 GB of DRAM traffic per launch let the SM clock sag to 1.5-1.75 GHz while
+//     phased launches held 1.85-1.95 GHz: 3 phases -14 % of the time (1 GPU, 17.6 GB gathered),
+//     -13 % at 8.8 GB (a rank of 2), -8 % at 4.4 GB (a rank of 4), a tie at 2.2 GB (a rank of 8);
+//     2 and 4 phases -10 %, 6 phases -4 %. In short bursts at the full clock the phased and
+//     unphased launches tie, so the phases cost nothing there.
+//   * B above 1.2x the L2: 160 MiB of B 3 phases -4 %, 256 MiB 4 phases -13 %, 512 MiB 8 phases
+//     -38 %, at >= 12 GB gathered; about one phase per half L2 of B.
 int auto_phases(const spmm_csr_view* A, int32_t N, const DeviceState* st) {
     if (st->l2_bytes <= 0) return 1;
     const double b_bytes = 4.0 * A->cols * static_cast<double>(N);
     const double gather_bytes = 4.0 * A->nnz * static_cast<double>(N);
     const double l2 = st->l2_bytes;
+    if (b_bytes > 0.8 * l2 && b_bytes <= 1.2 * l2) return gather_bytes >= 4e9 ? 3 : 1;
     if (b_bytes <= 1.2 * l2 || gather_bytes < 12e9) return 1;
     const int ph = static_cast<int>(b_bytes / (0.5 * l2) + 0.5);
     return std::min(std::max(ph, 1), 8);

@@ -86,6 +86,27 @@ def test_world_of_one_matches_oracle(cuda, case):
     plan.close()
 
 
+def test_phased_plan_runs_pipelined_and_matches(cuda):
+    # B of 128 MiB (131072 x 256, about the L2) and 4.3 GB of gathers: the plan takes 3 column
+    # phases for the resident launches; the pipelined end-to-end run launches its row groups
+    # unphased. Both must give the reference's chain bit for bit.
+    torch = cuda
+    A = S.generate_uniform_csr_fast(32768, 131072, 0.001, 42)
+    B = K.dense(131072, 256, 9)
+    plan = S.RankPlan(None, A, 256)
+    assert plan.algo == S.CSR_ROWWARP and plan.launches == 3
+    C = np.full((A.rows, 256), np.nan, np.float32)
+    plan.run(A, B, C)
+    for r0 in (0, 16384, 32768 - 512):
+        sl = S.row_slice(A, r0, r0 + 512)
+        assert bits_equal(C[r0:r0 + 512], O.spmm_csr_f32(K.to_oracle(sl), B)), r0
+    plan.execute()
+    assert bits_equal(device_rows(torch, plan.d_C, A.rows, 256), C)
+    code, detail = S.device_error(0)
+    assert code == 0, f"device error {code} at {detail}"
+    plan.close()
+
+
 def test_rank_slice_plans_match_reference_partition(cuda):
     # A world of one on each rank's slice gives that rank's rows: the split the multi-GPU path
     # takes is the reference's nnz-balanced one.
