@@ -335,11 +335,13 @@ int spmm_hybrid_run(const spmm_hybrid_plan* plan, const spmm_csr_view* hA, const
 /* (reference: src/spmm_multigpu.h:32, gpu_count) */
 int spmm_gpu_count(void);
 
-/* nnz-balanced row split over num_gpus devices (clamped to the visible count), B copied
- * to device 0 once and broadcast to the others with NCCL over NVLink, one host thread
- * per device, row-disjoint C gathered into hC. *time_ms = max over devices of the median
- * kernel time (the reference's semantics); *bcast_ms = the NCCL broadcast time.
- * rows_out / nnz_out (may be NULL) receive num_gpus entries.
+/* nnz-balanced row split over num_gpus devices (clamped to the visible count), one host thread
+ * per device running the per-rank path below (spmm_rank_run: each device copies its rows of A
+ * and 1/num_gpus of B's rows, an NCCL all-gather over NVLink completes B on every device, the
+ * rows of C come back into hC, row-disjoint). *time_ms = max over devices of the median kernel
+ * time on the resident operands (the reference's semantics); *bcast_ms = the time of the
+ * all-gather of B alone (max over devices). rows_out / nnz_out (may be NULL) receive
+ * num_gpus entries.
  * (reference: src/spmm_multigpu.h:49-52, spmm_multigpu; src/spmm_multigpu.cu:44-120) */
 int spmm_multigpu_run(const spmm_csr_view* hA, const float* hB, float* hC, int32_t N,
                       int32_t num_gpus, int32_t warmup, int32_t iters, float* time_ms,

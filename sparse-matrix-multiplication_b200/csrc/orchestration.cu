@@ -1,6 +1,6 @@
 // Host-side orchestration of libspmm_b200.so: the host-buffer end-to-end call, hybrid
-// CUDA-core / tensor-core dispatch, the multi-GPU row split with an NCCL broadcast of B,
-// and the managed-memory path.
+// CUDA-core / tensor-core dispatch, the single-process multi-GPU row split (a host thread per
+// device driving the per-rank path of multigpu_rank.cu), and the managed-memory path.
 //
 //   hybrid      src/spmm_hybrid.cu:28-125
 //   multi-GPU   src/spmm_multigpu.cu:44-120
@@ -10,6 +10,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <condition_variable>
 #include <cstring>
 #include <mutex>
 #include <thread>
@@ -417,105 +418,63 @@ int spmm_multigpu_run(const spmm_csr_view* hA, const float* hB, float* hC, int32
                       int32_t warmup, int32_t iters, float* time_ms, int32_t* used_gpus, int32_t* rows_out,
                       int32_t* nnz_out, float* bcast_ms) {
     if (!check_host_view(hA) || N < 0 || warmup < 0 || iters < 1 || !time_ms) return SPMM_ERR_INVALID_ARG;
+    if (hA->rows > 0 && hA->row_ptr[0] != 0) return SPMM_ERR_INVALID_ARG;
     const int visible = spmm_gpu_count();
     if (visible < 1) return SPMM_ERR_UNSUPPORTED;
-    int G = std::max(1, std::min(num_gpus, visible));
-    std::vector<int32_t> bounds(G + 1);
-    SPMM_TRY(spmm_nnz_balanced_bounds(hA->row_ptr, hA->rows, hA->nnz, G, bounds.data()));
-    const size_t K = hA->cols;
-    const size_t b_elems = K * static_cast<size_t>(N);
+    const int G = std::max(1, std::min(num_gpus, visible));
+    NvtxRange range("spmm_multigpu_run");
+    int prev_dev = 0;
+    cudaGetDevice(&prev_dev);
 
+    // One communicator per device, made in one call (this process drives every device), each
+    // wrapped for the per-rank entry points; with one device there is no exchange at all.
+    std::vector<ncclComm_t> comms;
+    std::vector<spmm_comm*> wrapped(G, nullptr);
+    int rc = SPMM_OK;
+    if (G > 1) {
+        const NcclApi& nc = nccl();
+        comms.assign(G, nullptr);
+        std::vector<int> devs(G);
+        for (int g = 0; g < G; ++g) devs[g] = g;
+        if (!nc.ranks_ok || nc.comm_init_all(comms.data(), G, devs.data()) != ncclSuccess) {
+            comms.clear();
+            rc = SPMM_ERR_NCCL;
+        }
+        for (int g = 0; g < G && rc == SPMM_OK; ++g) rc = spmm_comm_wrap(comms[g], 0, &wrapped[g]);
+    }
+
+    // One host thread per device, as the reference's worker (src/spmm_multigpu.cu:66-115), each
+    // running the per-rank path: its rows of A and its share of B's rows in, the all-gather of B
+    // over NVLink, the kernels, its rows of C back into hC; then the timed launches on the
+    // resident operands (the reference's per-GPU median) and the timed all-gather alone.
     struct Rank {
-        int dev = 0;
-        cudaStream_t s = nullptr;
-        float* dB = nullptr;
-        float* dC = nullptr;
-        void* ws = nullptr;
-        size_t ws_bytes = 0;
-        DeviceCsr A;
-        spmm_csr_host slice{};
-        float ms = 0.f;
+        float ms = 0.f, gather_ms = 0.f;
+        int32_t rows = 0, nnz = 0;
         int rc = SPMM_OK;
     };
     std::vector<Rank> ranks(G);
-    int rc = SPMM_OK;
-
-    // Set-up: per-device slice upload and buffers (outside the timing, as in the reference).
-    for (int g = 0; g < G && rc == SPMM_OK; ++g) {
-        Rank& R = ranks[g];
-        R.dev = g;
-        if (cudaSetDevice(g) != cudaSuccess || cudaStreamCreateWithFlags(&R.s, cudaStreamNonBlocking) != cudaSuccess) {
-            rc = SPMM_ERR_CUDA;
-            break;
-        }
-        rc = spmm_csr_row_slice_host(hA, bounds[g], bounds[g + 1], &R.slice);
-        if (rc != SPMM_OK) break;
-        spmm_csr_view sv{R.slice.rows, R.slice.cols, R.slice.nnz, R.slice.row_ptr, R.slice.col_idx, R.slice.values};
-        rc = upload_csr(&sv, &R.A, R.s);
-        if (rc != SPMM_OK) break;
-        if (cudaMalloc(&R.dB, sizeof(float) * std::max<size_t>(b_elems, 1)) != cudaSuccess ||
-            cudaMalloc(&R.dC, sizeof(float) * std::max<size_t>(static_cast<size_t>(sv.rows) * N, 1)) != cudaSuccess) {
-            rc = SPMM_ERR_NO_MEMORY;
-            break;
-        }
-        DeviceState* st = nullptr;
-        rc = device_state(g, &st);
-        if (rc != SPMM_OK) break;
-        rc = csr_f32_workspace_bytes(&sv, N, SPMM_CSR_AUTO, nullptr, st->sm_count, &R.ws_bytes);
-        if (rc != SPMM_OK) break;
-        if (R.ws_bytes) {
-            if (cudaMalloc(&R.ws, R.ws_bytes) != cudaSuccess) {
-                rc = SPMM_ERR_NO_MEMORY;
-                break;
-            }
-            cudaMemsetAsync(R.ws, 0, R.ws_bytes, R.s);
-        }
-    }
-
-    // B: one host->device copy to device 0, then an NCCL broadcast over NVLink.
-    float bcast = 0.f;
-    if (rc == SPMM_OK && b_elems) {
-        cudaSetDevice(0);
-        if (cudaMemcpyAsync(ranks[0].dB, hB, sizeof(float) * b_elems, cudaMemcpyHostToDevice, ranks[0].s) != cudaSuccess ||
-            cudaStreamSynchronize(ranks[0].s) != cudaSuccess)
-            rc = SPMM_ERR_CUDA;
-        if (rc == SPMM_OK && G > 1) {
-            const NcclApi& nc = nccl();
-            std::vector<ncclComm_t> comms(G);
-            std::vector<int> devs(G);
-            for (int g = 0; g < G; ++g) devs[g] = g;
-            if (!nc.ok || nc.comm_init_all(comms.data(), G, devs.data()) != ncclSuccess) {
-                rc = SPMM_ERR_NCCL;
+    // The threads meet before each collective step; if any of them failed, none enters it (a
+    // collective that one device never joins would otherwise wait for its timeout).
+    struct Meet {
+        std::mutex m;
+        std::condition_variable cv;
+        int n, arrived = 0, generation = 0;
+        bool failed = false;
+        explicit Meet(int count) : n(count) {}
+        bool all_ok(bool ok) {
+            std::unique_lock<std::mutex> lk(m);
+            failed = failed || !ok;
+            const int gen = generation;
+            if (++arrived == n) {
+                arrived = 0;
+                ++generation;
+                cv.notify_all();
             } else {
-                cudaEvent_t e0, e1;
-                cudaSetDevice(0);
-                cudaEventCreate(&e0);
-                cudaEventCreate(&e1);
-                cudaEventRecord(e0, ranks[0].s);
-                bool ok = nc.group_start() == ncclSuccess;
-                for (int g = 0; g < G && ok; ++g) {
-                    cudaSetDevice(g);
-                    // The send buffer is read on the root only.
-                    ok = nc.broadcast(ranks[g].dB, ranks[g].dB, b_elems, ncclFloat, 0, comms[g], ranks[g].s) == ncclSuccess;
-                }
-                ok = (nc.group_end() == ncclSuccess) && ok;
-                cudaSetDevice(0);
-                cudaEventRecord(e1, ranks[0].s);
-                for (int g = 0; g < G; ++g) {
-                    cudaSetDevice(g);
-                    if (cudaStreamSynchronize(ranks[g].s) != cudaSuccess) ok = false;
-                }
-                cudaSetDevice(0);
-                cudaEventElapsedTime(&bcast, e0, e1);
-                cudaEventDestroy(e0);
-                cudaEventDestroy(e1);
-                for (int g = 0; g < G; ++g) nc.comm_destroy(comms[g]);
-                if (!ok) rc = SPMM_ERR_NCCL;
+                cv.wait(lk, [&] { return generation != gen; });
             }
+            return !failed;
         }
-    }
-
-    // One host thread per device: warm-up, timed launches, gather of the row slice.
+    } meet(G);
     if (rc == SPMM_OK) {
         std::vector<std::thread> pool;
         for (int g = 0; g < G; ++g) {
@@ -525,48 +484,51 @@ int spmm_multigpu_run(const spmm_csr_view* hA, const float* hB, float* hC, int32
                     R.rc = SPMM_ERR_CUDA;
                     return;
                 }
-                DeviceState* st = nullptr;
-                R.rc = device_state(g, &st);
-                if (R.rc != SPMM_OK) return;
-                if (R.A.view.rows > 0) {
-                    R.rc = time_launches(
-                        [&] {
-                            return csr_f32_launch(&R.A.view, R.dB, R.dC, N, SPMM_CSR_AUTO, nullptr, R.ws, R.ws_bytes,
-                                                  R.s, st);
-                        },
-                        warmup, iters, R.s, &R.ms);
-                    if (R.rc == SPMM_OK &&
-                        cudaMemcpyAsync(hC + static_cast<size_t>(bounds[g]) * N, R.dC,
-                                        sizeof(float) * static_cast<size_t>(R.A.view.rows) * N, cudaMemcpyDeviceToHost,
-                                        R.s) != cudaSuccess)
-                        R.rc = SPMM_ERR_CUDA;
-                    if (R.rc == SPMM_OK && cudaStreamSynchronize(R.s) != cudaSuccess) R.rc = SPMM_ERR_CUDA;
+                cudaStream_t s = nullptr;
+                if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
+                    R.rc = SPMM_ERR_CUDA;
+                    return;
                 }
+                spmm_rank_plan* plan = nullptr;
+                R.rc = spmm_rank_plan_create(wrapped[g], hA, N, s, &plan);
+                int32_t r0 = 0, r1 = 0;
+                if (meet.all_ok(R.rc == SPMM_OK)) {
+                    spmm_rank_plan_info(plan, &r0, &r1, &R.nnz, nullptr, nullptr, nullptr, nullptr);
+                    R.rows = r1 - r0;
+                    R.rc = spmm_rank_run(plan, hA, hB, hC + static_cast<size_t>(r0) * N, s);
+                    if (meet.all_ok(R.rc == SPMM_OK) && G > 1)
+                        R.rc = time_launches([&] { return spmm_rank_gather_b(plan, s); }, 1, 3, s, &R.gather_ms);
+                } else if (R.rc == SPMM_OK) {
+                    R.rc = SPMM_ERR_INVALID_ARG;  // another device failed: this one stops too
+                }
+                if (R.rc == SPMM_OK && R.rows > 0)
+                    R.rc = time_launches([&] { return spmm_rank_execute(plan, s); }, warmup, iters, s, &R.ms);
+                cudaStreamSynchronize(s);
+                spmm_rank_plan_destroy(plan);
+                cudaStreamDestroy(s);
             });
         }
         for (auto& t : pool) t.join();
         for (int g = 0; g < G; ++g)
             if (ranks[g].rc != SPMM_OK && rc == SPMM_OK) rc = ranks[g].rc;
     }
-
-    float worst = 0.f;
-    for (int g = 0; g < G; ++g) {
-        Rank& R = ranks[g];
-        worst = std::max(worst, R.ms);
-        if (rows_out) rows_out[g] = bounds[g + 1] - bounds[g];
-        if (nnz_out) nnz_out[g] = R.slice.nnz;
+    for (spmm_comm* w : wrapped) spmm_comm_destroy(w);
+    for (int g = 0; g < static_cast<int>(comms.size()); ++g) {
         cudaSetDevice(g);
-        if (R.s) cudaStreamSynchronize(R.s);
-        cudaFree(R.dB);
-        cudaFree(R.dC);
-        cudaFree(R.ws);
-        if (R.s) cudaStreamDestroy(R.s);
-        spmm_csr_host_free(&R.slice);
+        if (comms[g]) nccl().comm_destroy(comms[g]);
     }
-    cudaSetDevice(0);
+    cudaSetDevice(prev_dev);
+
+    float worst = 0.f, gather = 0.f;
+    for (int g = 0; g < G; ++g) {
+        worst = std::max(worst, ranks[g].ms);
+        gather = std::max(gather, ranks[g].gather_ms);
+        if (rows_out) rows_out[g] = ranks[g].rows;
+        if (nnz_out) nnz_out[g] = ranks[g].nnz;
+    }
     *time_ms = worst;
     if (used_gpus) *used_gpus = G;
-    if (bcast_ms) *bcast_ms = bcast;
+    if (bcast_ms) *bcast_ms = gather;
     return rc;
 }
 

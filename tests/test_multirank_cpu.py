@@ -1,9 +1,10 @@
-"""The multi-rank host logic of bench.py on CPU ranks (gloo, world_size 2 and 3): every rank
-builds the same A, takes the reference's nnz-balanced row range, receives B by broadcast from
-rank 0, computes its rows (the CPU oracle stands in for the GPU kernel here) and the gathered
-rows equal the single-process product bit for bit. A second test drops a rank before the
-broadcast and checks the survivor gets an error from the short process-group timeout instead
-of hanging."""
+"""The data flow of the per-rank multi-GPU path (spmm_rank_run) on CPU ranks (gloo, world_size 2
+and 3): every rank builds the same A and B, takes the reference's nnz-balanced row range, holds
+only its share of B's rows (rows K*r/world .. K*(r+1)/world, the library's split; unequal when
+world does not divide K), the ranks all-gather the shares into the whole B, each computes its
+rows (the CPU oracle stands in for the GPU kernel here) and the gathered rows equal the
+single-process product bit for bit. A second test drops a rank before the exchange and checks
+the survivor gets an error from the short process-group timeout instead of hanging."""
 from __future__ import annotations
 
 import os
@@ -35,8 +36,17 @@ def _shard_worker(rank: int, world: int, port: int, out_dir: str):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     A = S.generate_uniform_csr(3000, 2000, 0.01, 42)
-    B = torch.from_numpy(S.generate_dense(2000, 48, 43)) if rank == 0 else torch.zeros(2000, 48)
-    dist.broadcast(B, src=0)
+    K = 2000
+    full_b = S.generate_dense(K, 48, 43)
+    # This rank's share of B's rows, then an all-gather of the shares (padded to the largest
+    # share, as gloo's all_gather wants equal sizes) into the whole B.
+    share = [K * r // world for r in range(world + 1)]
+    mine = torch.zeros(max(share[r + 1] - share[r] for r in range(world)), 48)
+    mine[: share[rank + 1] - share[rank]] = torch.from_numpy(full_b[share[rank]:share[rank + 1]])
+    parts_b = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(parts_b, mine)
+    B = torch.cat([parts_b[r][: share[r + 1] - share[r]] for r in range(world)])
+    assert np.array_equal(B.numpy(), full_b)
     bounds = S.nnz_balanced_bounds(A.row_ptr, A.rows, A.nnz, world)
     sl = S.row_slice(A, int(bounds[rank]), int(bounds[rank + 1]))
     Cr = O.spmm_csr_f32(O.CSR(sl.rows, sl.cols, sl.row_ptr, sl.col_idx, sl.values), B.numpy())
