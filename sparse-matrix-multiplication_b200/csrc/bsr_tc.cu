@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdint>
 #include <mutex>
@@ -55,6 +56,11 @@ struct spmm_bsr_plan {
     int32_t device = 0;
     bool tc = false;
     CUtensorMap ta{};
+    // B's tensor map for the last B16 pointer executed (re-encoded only when B16 changes: the
+    // encode is host work between the caller's launch and the kernel's start).
+    mutable std::mutex tb_mu;
+    mutable CUtensorMap tb{};
+    mutable const void* tb_for = nullptr;
 };
 
 namespace spmm_b200 {
@@ -326,13 +332,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         while (ok && !done) {
             int nb = 0;
             if constexpr (SCHED) {
-                // The batch's entries, one per lane, straight from the schedule.
+                // The batch's entries, one per lane, straight from the schedule. They are loaded
+                // before the step count is known (one dependent memory round trip fewer before the
+                // first copy is issued): the schedule is padded by a batch of entries past its
+                // last record, so these loads stay inside it; entries past the count are ignored.
+                int e_bc = 0, e_mask = 0, e_blk[G];
+                if (lane < kStages) {
+                    const int* e = my_sched + 2 + (step + lane) * (2 + G);
+                    e_bc = __ldg(e);
+                    e_mask = __ldg(e + 1);
+#pragma unroll
+                    for (int j = 0; j < G; ++j) e_blk[j] = __ldg(e + 2 + j);
+                }
                 nb = min(kStages, total_steps - step);
                 if (lane < nb) {
-                    const int* e = my_sched + 2 + (step + lane) * (2 + G);
-                    sched_bc[lane] = __ldg(e);
-                    sched_mask[lane] = __ldg(e + 1);
-                    for (int j = 0; j < G; ++j) sched_blk[lane * G + j] = __ldg(e + 2 + j);
+                    sched_bc[lane] = e_bc;
+                    sched_mask[lane] = e_mask;
+#pragma unroll
+                    for (int j = 0; j < G; ++j) sched_blk[lane * G + j] = e_blk[j];
                 }
                 done = step + nb >= total_steps;
             }
@@ -595,9 +612,17 @@ int encode_a_map(CUtensorMap* ta, const BsrArgs& a) {
 template <int G, bool SCHED>
 int launch_tc_maps(const BsrArgs& a, const CUtensorMap& tb, const CUtensorMap& ta, cudaStream_t s) {
     using L = Layout<G>;
-    // Per device (the attribute belongs to the current device's context).
-    SPMM_CUDA_TRY(
-        cudaFuncSetAttribute(bsr_tcgen05_kernel<G, SCHED>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamic));
+    // The shared-memory attribute belongs to the current device's context: set it once per
+    // device (a bit per device id), not on every launch.
+    static std::atomic<unsigned long long> attr_set{0};
+    int dev = 0;
+    SPMM_CUDA_TRY(cudaGetDevice(&dev));
+    const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+    if (!bit || !(attr_set.load(std::memory_order_acquire) & bit)) {
+        SPMM_CUDA_TRY(cudaFuncSetAttribute(bsr_tcgen05_kernel<G, SCHED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           L::kDynamic));
+        attr_set.fetch_or(bit, std::memory_order_acq_rel);
+    }
     const dim3 grid((a.block_rows + G - 1) / G, (a.N + 127) / 128);
     bsr_tcgen05_kernel<G, SCHED><<<grid, kTcThreads, L::kDynamic, s>>>(tb, ta, a);
     SPMM_CUDA_TRY(cudaGetLastError());
@@ -773,10 +798,15 @@ int spmm_bsr16_plan_create(const spmm_bsr_view* A, int32_t N, void* stream, spmm
         // A schedule of at most 256 MiB; beyond that the kernel merges on the fly.
         if (rc == SPMM_OK) {
             p->stride = 2 + p->max_steps * (2 + p->group);
-            const size_t bytes = sizeof(int) * static_cast<size_t>(groups) * static_cast<size_t>(p->stride);
+            // Padded by one batch of entries: the kernel loads a batch before it knows how many
+            // of its entries are real.
+            const size_t bytes = sizeof(int) * (static_cast<size_t>(groups) * static_cast<size_t>(p->stride) +
+                                                static_cast<size_t>(kStages) * (2 + p->group));
             if (bytes <= (256ull << 20)) {
                 if (cudaMalloc(&p->sched, bytes) != cudaSuccess) {
                     rc = SPMM_ERR_NO_MEMORY;
+                } else if (cudaMemsetAsync(p->sched, 0, bytes, s) != cudaSuccess) {
+                    rc = SPMM_ERR_CUDA;
                 } else {
                     p->sched_bytes = bytes;
                     if (p->group == 8) bsr_schedule_kernel<8><<<blocks, 256, 0, s>>>(a, p->sched, p->stride, nullptr, 0);
@@ -820,7 +850,14 @@ int spmm_bsr16_plan_execute(const spmm_bsr_plan* p, const void* B16, float* C, v
     a.sched = p->sched;
     a.sched_stride = p->stride;
     CUtensorMap tb;
-    SPMM_TRY(encode_b_map(&tb, a));
+    {
+        std::lock_guard<std::mutex> lock(p->tb_mu);
+        if (p->tb_for != B16) {
+            SPMM_TRY(encode_b_map(&p->tb, a));
+            p->tb_for = B16;
+        }
+        tb = p->tb;
+    }
     if (p->group == 8) return launch_tc_maps<8, true>(a, tb, p->ta, s);
     return launch_tc_maps<4, true>(a, tb, p->ta, s);
 }
