@@ -399,6 +399,8 @@ int spmm_rank_plan_info(const spmm_rank_plan* plan, int32_t* row_begin, int32_t*
  * caller that holds the whole M x N C passes C + row_begin * N). hA must be the matrix the plan
  * was made for: its values may change between calls, its structure may not (a row_ptr that
  * differs at the rank's boundaries is refused). hB is the whole K x N B.
+ * With SPMM_B200_B_PIECES=P (2..16) in the environment when the plan is made, the share is copied
+ * in P pieces and each piece goes to the other ranks (grouped send/recv) as soon as it has landed.
  * Pipelined (one-warp-per-row plans): the all-gather overlaps the copy of A's rows, each of 8
  * nnz-balanced row groups is launched once its rows have landed, and each group's rows of C go
  * back while later groups compute. Bit-identical to spmm_rank_execute and to spmm_csr_f32 with

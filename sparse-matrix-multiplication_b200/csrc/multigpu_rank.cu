@@ -16,6 +16,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <thread>
@@ -38,6 +39,21 @@ namespace spmm_b200 {
 namespace {
 
 constexpr int kRankGroups = 8;  // row groups of one rank's pipelined run
+// Pieces of a rank's B share in an end-to-end run (world > 1). One piece: the share crosses the
+// host link, then one ncclAllGather (or grouped send/recv for unequal shares) completes B. More
+// pieces: each piece is sent to every other rank (grouped send/recv) as soon as it has landed,
+// while the next piece is still being copied.
+constexpr int kBPieces = 1;
+
+// Pieces of B's share per end-to-end run: SPMM_B200_B_PIECES (1..16) when set, else kBPieces.
+int b_pieces_setting() {
+    const char* e = std::getenv("SPMM_B200_B_PIECES");
+    if (e && e[0]) {
+        const int v = std::atoi(e);
+        if (v >= 1 && v <= 16) return v;
+    }
+    return kBPieces;
+}
 
 using Clock = std::chrono::steady_clock;
 
@@ -133,10 +149,11 @@ struct spmm_rank_plan {
     spmm_csr_plan* cplan = nullptr;
     int32_t algo = SPMM_CSR_ROWWARP;
     int32_t k_phases = 1;
+    int32_t b_pieces = 1;  // pieces of the B share copied and exchanged one after another
     bool pipelined = false;
     cudaStream_t s_in = nullptr, s_comm = nullptr, s_k = nullptr, s_out = nullptr;
     // [0] start, [1] B share landed, [2] B gathered, [3 + g] rows of group g landed,
-    // [3 + G + g] group g computed, [3 + 2G] end.
+    // [3 + G + g] group g computed, [3 + 2G] end, [4 + 2G + j] piece j of the B share landed.
     std::vector<cudaEvent_t> ev;
 
     int rows() const { return r1 - r0; }
@@ -218,6 +235,44 @@ int gather_b_issue(spmm_rank_plan* p, cudaStream_t s) {
     return end == ncclInProgress ? wait_comm_ready(c) : SPMM_OK;
 }
 
+// Rows [lo, hi) of piece j of rank r's share of B (the share cut into P near-equal pieces).
+void share_piece(const spmm_rank_plan* p, int r, int j, int P, int32_t* lo, int32_t* hi) {
+    const int64_t b0 = p->b_bounds[r], len = p->b_bounds[r + 1] - b0;
+    *lo = static_cast<int32_t>(b0 + len * j / P);
+    *hi = static_cast<int32_t>(b0 + len * (j + 1) / P);
+}
+
+// Piece j of every rank's share to every other rank (point-to-point, grouped), on `s`: the
+// exchange of a piece starts as soon as this rank's copy of it has landed, while the next
+// piece is still crossing the host link.
+int exchange_piece_issue(spmm_rank_plan* p, int j, int P, cudaStream_t s) {
+    spmm_comm* c = p->comm;
+    if (c->broken) return SPMM_ERR_NCCL;
+    const NcclApi& nc = nccl();
+    const size_t N = static_cast<size_t>(p->N);
+    int32_t mlo = 0, mhi = 0;
+    share_piece(p, p->rank, j, P, &mlo, &mhi);
+    const size_t mine = static_cast<size_t>(mhi - mlo) * N;
+    NvtxRange range("spmm_rank: exchange B piece");
+    if (nc.group_start() != ncclSuccess) return SPMM_ERR_NCCL;
+    bool ok = true;
+    for (int r = 0; r < p->world && ok; ++r) {
+        if (r == p->rank) continue;
+        int32_t lo = 0, hi = 0;
+        share_piece(p, r, j, P, &lo, &hi);
+        const size_t theirs = static_cast<size_t>(hi - lo) * N;
+        if (mine) ok = nc.send(p->d_B + static_cast<size_t>(mlo) * N, mine, ncclFloat, r, c->comm, s) == ncclSuccess;
+        if (ok && theirs)
+            ok = nc.recv(p->d_B + static_cast<size_t>(lo) * N, theirs, ncclFloat, r, c->comm, s) == ncclSuccess;
+    }
+    const ncclResult_t end = nc.group_end();
+    if (!ok || (end != ncclSuccess && end != ncclInProgress)) {
+        abort_comm(c);
+        return SPMM_ERR_NCCL;
+    }
+    return end == ncclInProgress ? wait_comm_ready(c) : SPMM_OK;
+}
+
 int run_issue(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float* hC, cudaStream_t s,
               DeviceState* st) {
     const size_t N = static_cast<size_t>(p->N);
@@ -225,19 +280,33 @@ int run_issue(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float
     cudaEvent_t* ev = p->ev.data();
     SPMM_CUDA_TRY(cudaEventRecord(ev[0], s));
     for (cudaStream_t x : {p->s_in, p->s_comm, p->s_k, p->s_out}) SPMM_CUDA_TRY(cudaStreamWaitEvent(x, ev[0], 0));
+    const int P = p->b_pieces;
+    cudaEvent_t* ev_piece = ev + 4 + 2 * G;
     {
-        // B first: the all-gather can start once every rank's share has landed.
+        // B first, in P pieces: the exchange of B can start once every rank's piece has landed,
+        // and with P > 1 the exchange of one piece overlaps the host copy of the next.
         NvtxRange range("spmm_rank: B share H2D");
-        const int32_t b0 = p->b_bounds[p->rank], b1 = p->b_bounds[p->rank + 1];
-        if (static_cast<size_t>(b1 - b0) * N != 0)
-            SPMM_CUDA_TRY(cudaMemcpyAsync(p->d_B + static_cast<size_t>(b0) * N, hB + static_cast<size_t>(b0) * N,
-                                          sizeof(float) * static_cast<size_t>(b1 - b0) * N, cudaMemcpyHostToDevice,
-                                          p->s_in));
+        for (int j = 0; j < P; ++j) {
+            int32_t lo = 0, hi = 0;
+            share_piece(p, p->rank, j, P, &lo, &hi);
+            if (static_cast<size_t>(hi - lo) * N != 0)
+                SPMM_CUDA_TRY(cudaMemcpyAsync(p->d_B + static_cast<size_t>(lo) * N, hB + static_cast<size_t>(lo) * N,
+                                              sizeof(float) * static_cast<size_t>(hi - lo) * N, cudaMemcpyHostToDevice,
+                                              p->s_in));
+            SPMM_CUDA_TRY(cudaEventRecord(ev_piece[j], p->s_in));
+        }
         SPMM_CUDA_TRY(cudaEventRecord(ev[1], p->s_in));
     }
     if (p->world > 1) {
-        SPMM_CUDA_TRY(cudaStreamWaitEvent(p->s_comm, ev[1], 0));
-        SPMM_TRY(gather_b_issue(p, p->s_comm));
+        if (P == 1) {
+            SPMM_CUDA_TRY(cudaStreamWaitEvent(p->s_comm, ev[1], 0));
+            SPMM_TRY(gather_b_issue(p, p->s_comm));
+        } else {
+            for (int j = 0; j < P; ++j) {
+                SPMM_CUDA_TRY(cudaStreamWaitEvent(p->s_comm, ev_piece[j], 0));
+                SPMM_TRY(exchange_piece_issue(p, j, P, p->s_comm));
+            }
+        }
         SPMM_CUDA_TRY(cudaEventRecord(ev[2], p->s_comm));
     } else {
         SPMM_CUDA_TRY(cudaEventRecord(ev[2], p->s_in));
@@ -476,7 +545,8 @@ int spmm_rank_plan_create(spmm_comm* comm, const spmm_csr_view* hA, int32_t N, v
     for (int g = 0; g <= G; ++g) p->group_pos[g] = rp[p->groups[g]];
     for (cudaStream_t* x : {&p->s_in, &p->s_comm, &p->s_k, &p->s_out})
         if (cudaStreamCreateWithFlags(x, cudaStreamNonBlocking) != cudaSuccess) return fail(SPMM_ERR_CUDA);
-    p->ev.assign(4 + 2 * G, nullptr);
+    p->b_pieces = p->world > 1 ? b_pieces_setting() : 1;
+    p->ev.assign(4 + 2 * G + p->b_pieces, nullptr);
     for (auto& e : p->ev)
         if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return fail(SPMM_ERR_CUDA);
     *out = p;

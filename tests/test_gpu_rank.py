@@ -171,12 +171,12 @@ _CHILD = textwrap.dedent("""
 """)
 
 
-def _spawn(tmp_path, world: int, devices, job: dict, timeout: int = 240):
+def _spawn(tmp_path, world: int, devices, job: dict, timeout: int = 240, pieces: int = 1):
     job_path = tmp_path / "job.pkl"
     job_path.write_bytes(pickle.dumps(job))
     script = tmp_path / "child.py"
     script.write_text(_CHILD.format(repo=str(REPO)))
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SPMM_B200_B_PIECES=str(pieces))
     procs = [subprocess.Popen([sys.executable, str(script), str(r), str(world), str(devices[r]),
                                str(tmp_path / f"out{r}.pkl"), str(job_path)], env=env)
              for r in range(len(devices))]
@@ -186,14 +186,16 @@ def _spawn(tmp_path, world: int, devices, job: dict, timeout: int = 240):
     return [pickle.loads((tmp_path / f"out{r}.pkl").read_bytes()) for r in range(len(devices))]
 
 
-@pytest.mark.parametrize("K_rows", [4096, 4093])
-def test_two_ranks_gather_b_and_return_their_rows(cuda, tmp_path, K_rows):
+@pytest.mark.parametrize("K_rows,pieces", [(4096, 1), (4093, 1), (4096, 4), (4093, 3)])
+def test_two_ranks_gather_b_and_return_their_rows(cuda, tmp_path, K_rows, pieces):
     if S.gpu_count() < 2:
         pytest.skip("needs 2 GPUs")
-    # K_rows = 4093 gives unequal B shares (grouped send/recv instead of ncclAllGather).
+    # K_rows = 4093 gives unequal B shares (grouped send/recv instead of ncclAllGather); pieces > 1
+    # exchanges each share piece by piece while the next piece is being copied.
     A = S.generate_uniform_csr(8192, K_rows, 0.01, 42)
     B = S.generate_dense(K_rows, 128, 43)
-    res = _spawn(tmp_path, 2, [0, 1], {"id": S.comm_unique_id(), "timeout_ms": 120000, "A": A, "B": B})
+    res = _spawn(tmp_path, 2, [0, 1], {"id": S.comm_unique_id(), "timeout_ms": 120000, "A": A, "B": B},
+                 pieces=pieces)
     bounds = S.nnz_balanced_bounds(A.row_ptr, A.rows, A.nnz, 2)
     for r, d in enumerate(res):
         assert d["rows"] == (int(bounds[r]), int(bounds[r + 1]))
