@@ -90,6 +90,8 @@ def test_multigpu_row_split(cuda, gpus):
     for k in range(g):
         sl = S.row_slice(A, int(bounds[k]), int(bounds[k + 1]))
         assert r["nnz"][k] == sl.nnz
-        assert bits_equal(C[bounds[k]:bounds[k + 1]], split_oracle(sl, B))
+        # Every device runs the per-rank path, whose plan takes one warp per row for this
+        # uniform matrix: the reference's sequential FMA chain for every element.
+        assert bits_equal(C[bounds[k]:bounds[k + 1]], O.spmm_csr_f32(K.to_oracle(sl), B))
     if g > 1:
         assert r["bcast_ms"] > 0
