@@ -14,9 +14,11 @@ over NVLink, and each rank computes its rows of C -- the total work is fixed ("s
 One step = one SpMM of the rank's row range, inputs resident in HBM (spmm_rank_execute). `value`
 is whole-job GFLOP/s, 2*nnz*N / (max over ranks of the device time of the K timed steps / K).
 The inputs (406 MB at N=1) are larger than the 126 MB L2, so no flush is needed between steps.
-`e2e` is the same metric through spmm_rank_run on pinned host buffers: per step, every rank copies
-its rows of A and its 1/N share of B's rows in, the ranks all-gather B over NVLink, the kernels
-run and each rank's rows of C come back -- pipelined inside the library. Both are timed with CUDA
+`e2e` is the same metric from pinned host buffers: per step, every rank copies its rows of A and
+its 1/N share of B's rows in, the ranks all-gather B over NVLink, the kernels run and each rank's
+rows of C come back -- pipelined inside the library. Its `value` submits the steps back to back
+(spmm_rank_submit, one spmm_rank_wait at the end: a step's copy back overlaps the next step's
+copies in); `e2e.sync` times one synchronous spmm_rank_run per step. All are timed with CUDA
 events on the launching stream, max over ranks.
 
 After the timed regions every rank checks its rows of C from the last end-to-end step against the
@@ -436,20 +438,40 @@ def run_csr(args, torch, dist, R: Ranks, rank: int, world: int, local: int) -> d
     total_flops = 2.0 * R.sum(float(plan.nnz)) * N
     value = total_flops / (ms_step * 1e-3) / 1e9
 
-    # ---- end to end through spmm_rank_run (host buffers, copies inside the timed region)
+    # ---- end to end from host buffers (copies inside the timed region). Throughput: ke steps
+    # submitted back to back (spmm_rank_submit, alternating between two pinned C buffers), one
+    # wait, so a step's copy back of C shares the host link with the next step's copies in;
+    # latency: ke synchronous spmm_rank_run calls.
     e2e = None
     if not args.no_e2e:
+        hC2 = torch.empty((max(rows_r, 1), N), dtype=torch.float32).pin_memory().numpy()
         for _ in range(2):
             plan.run(hA, hB, hC, stream)
         ke = max(3, min(K, 20))
-        ms_e2e_rank, _ = time_steps(torch, lambda: plan.run(hA, hB, hC, stream), ke, stream, None, R)
-        e2e_ms = R.max(ms_e2e_rank)
+        ms_sync_rank, _ = time_steps(torch, lambda: plan.run(hA, hB, hC, stream), ke, stream, None, R)
+        bufs = (hC2, hC)  # the last submitted step writes hC, which the parity check reads
+        hC.fill(np.nan)
+        R.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(ke):
+            plan.submit(hA, hB, bufs[(i + ke) % 2], stream)
+        plan.wait(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        R.barrier()
+        e2e_ms = R.max(t0.elapsed_time(t1) / ke)
+        sync_ms = R.max(ms_sync_rank)
         h2d = R.sum(float(4 * (rows_r + 1) + 8 * plan.nnz + 4 * (plan.b_row_end - plan.b_row_begin) * N))
         d2h = R.sum(float(4 * rows_r * N))
         e2e = {"value": round(total_flops / (e2e_ms * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "api": "spmm_rank_run (C ABI; per rank: its A rows and 1/N of B's rows H2D from pinned buffers, "
-                      "NCCL all-gather of B over NVLink, kernels, its C rows D2H; pipelined in row groups)"}
+               "api": "spmm_rank_submit x steps + spmm_rank_wait (C ABI; per rank and step: its A rows and 1/N of "
+                      "B's rows H2D from pinned buffers, NCCL all-gather of B over NVLink, kernels, its C rows D2H; "
+                      "pipelined in row groups, consecutive steps overlapped)",
+               "sync": {"value": round(total_flops / (sync_ms * 1e-3) / 1e9, 3), "ms_per_step": round(sync_ms, 4),
+                        "api": "spmm_rank_run per step (returns when the step's C is on the host)"}}
     else:
         plan.run(hA, hB, hC, stream)
     torch.cuda.synchronize()

@@ -408,8 +408,22 @@ int spmm_rank_plan_info(const spmm_rank_plan* plan, int32_t* row_begin, int32_t*
  * bounded by the communicator's timeout). Pinned host buffers make the copies asynchronous. */
 int spmm_rank_run(spmm_rank_plan* plan, const spmm_csr_view* hA, const float* hB, float* hC_rows, void* stream);
 
+/* spmm_rank_run without the wait, for a stream of multiplies: issues the same copies, exchange,
+ * kernels and copies back, and returns. The next run or submit on the plan overlaps this one where
+ * the buffers allow: its copies in wait only for this run's kernels, its kernels for this run's
+ * copies back, so one run's copies back can share the host links with the next run's copies in.
+ * hA, hB and hC_rows must stay valid and unchanged, and hC_rows is not written in full, until
+ * spmm_rank_wait returns (give consecutive submits different hC_rows). Collective, like
+ * spmm_rank_run. (no counterpart in the reference, whose multi-GPU call is synchronous) */
+int spmm_rank_submit(spmm_rank_plan* plan, const spmm_csr_view* hA, const float* hB, float* hC_rows, void* stream);
+
+/* Waits (bounded by the communicator's timeout) until the last run issued on the plan has put its
+ * rows of C on the host, and makes `stream` wait for it too. */
+int spmm_rank_wait(spmm_rank_plan* plan, void* stream);
+
 /* The kernels alone, on the device-resident operands the last spmm_rank_run left behind (the
- * rank's rows of A and the gathered B), into the plan's device C. Asynchronous, not collective. */
+ * rank's rows of A and the gathered B), into the plan's device C. Asynchronous, not collective.
+ * After spmm_rank_submit, call spmm_rank_wait first. */
 int spmm_rank_execute(spmm_rank_plan* plan, void* stream);
 
 /* The all-gather of B alone (device to device over NVLink, from the shares already on every

@@ -156,9 +156,16 @@ struct spmm_rank_plan {
     // [3 + G + g] group g computed, [3 + 2G] end, [4 + 2G + j] piece j of the B share landed.
     std::vector<cudaEvent_t> ev;
 
+    // Cross-step ordering of submitted runs: a run's copies into the device buffers wait for the
+    // previous run's kernels (kdone), its kernels for the previous run's copies back (end).
+    cudaEvent_t kdone = nullptr;
+    bool submitted = false;  // a run has been issued since the plan was made
+
     int rows() const { return r1 - r0; }
     int nnz() const { return p1 - p0; }
     int timeout_ms() const { return comm ? comm->timeout_ms : 300000; }
+    int groups_count() const { return static_cast<int>(groups.size()) - 1; }
+    cudaEvent_t end_event() const { return ev[3 + 2 * groups_count()]; }
 };
 
 namespace spmm_b200 {
@@ -174,6 +181,7 @@ void release(spmm_rank_plan* p) {
     if (p->cplan) spmm_csr_plan_destroy(p->cplan);
     for (cudaEvent_t e : p->ev)
         if (e) cudaEventDestroy(e);
+    if (p->kdone) cudaEventDestroy(p->kdone);
     for (cudaStream_t s : {p->s_in, p->s_comm, p->s_k, p->s_out})
         if (s) cudaStreamDestroy(s);
     cudaFree(p->d_rp);
@@ -273,13 +281,34 @@ int exchange_piece_issue(spmm_rank_plan* p, int j, int P, cudaStream_t s) {
     return end == ncclInProgress ? wait_comm_ready(c) : SPMM_OK;
 }
 
+int check_plan_device(const spmm_rank_plan* p) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return SPMM_ERR_UNSUPPORTED;
+    }
+    return dev == p->device ? SPMM_OK : SPMM_ERR_INVALID_ARG;
+}
+
+// Issues one end-to-end run. `join`: the caller's stream waits for the run's last copy back
+// (spmm_rank_run); without it (spmm_rank_submit) the caller's stream is only the run's start,
+// so that the next submitted run's copies in can overlap this run's copies back.
 int run_issue(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float* hC, cudaStream_t s,
-              DeviceState* st) {
+              DeviceState* st, bool join) {
     const size_t N = static_cast<size_t>(p->N);
-    const int G = static_cast<int>(p->groups.size()) - 1;
+    const int G = p->groups_count();
     cudaEvent_t* ev = p->ev.data();
+    const bool prev = p->submitted;
     SPMM_CUDA_TRY(cudaEventRecord(ev[0], s));
     for (cudaStream_t x : {p->s_in, p->s_comm, p->s_k, p->s_out}) SPMM_CUDA_TRY(cudaStreamWaitEvent(x, ev[0], 0));
+    // The device buffers this run overwrites are still read by the previous run's kernels
+    // (A's rows, B) and copies back (C): wait for those, not for the whole previous run.
+    if (prev) {
+        SPMM_CUDA_TRY(cudaStreamWaitEvent(p->s_in, p->kdone, 0));
+        SPMM_CUDA_TRY(cudaStreamWaitEvent(p->s_comm, p->kdone, 0));
+        SPMM_CUDA_TRY(cudaStreamWaitEvent(p->s_k, p->end_event(), 0));
+    }
+    p->submitted = true;
     const int P = p->b_pieces;
     cudaEvent_t* ev_piece = ev + 4 + 2 * G;
     {
@@ -354,6 +383,7 @@ int run_issue(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float
             }
             SPMM_CUDA_TRY(cudaEventRecord(ev[3 + G + g], p->s_k));
         }
+        SPMM_CUDA_TRY(cudaEventRecord(p->kdone, p->s_k));
     }
     {
         NvtxRange range("spmm_rank: C rows D2H");
@@ -366,18 +396,37 @@ int run_issue(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float
                                               p->s_out));
         }
         SPMM_CUDA_TRY(cudaEventRecord(ev[3 + 2 * G], p->s_out));
-        SPMM_CUDA_TRY(cudaStreamWaitEvent(s, ev[3 + 2 * G], 0));
+        if (join) SPMM_CUDA_TRY(cudaStreamWaitEvent(s, ev[3 + 2 * G], 0));
     }
     return SPMM_OK;
 }
 
-int check_plan_device(const spmm_rank_plan* p) {
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess) {
-        cudaGetLastError();
-        return SPMM_ERR_UNSUPPORTED;
+int check_run_args(const spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, const float* hC_rows) {
+    if (!p || !host_view_ok(hA)) return SPMM_ERR_INVALID_ARG;
+    if (hA->rows != p->M || hA->cols != p->K || hA->nnz != p->nnz_all || hA->row_ptr[p->r0] != p->p0 ||
+        hA->row_ptr[p->r1] != p->p1)
+        return SPMM_ERR_INVALID_ARG;  // not the matrix the plan was made for
+    const size_t N = static_cast<size_t>(p->N);
+    if ((static_cast<size_t>(p->K) * N != 0 && !hB) || (static_cast<size_t>(p->rows()) * N != 0 && !hC_rows))
+        return SPMM_ERR_INVALID_ARG;
+    if (p->comm && p->comm->broken) return SPMM_ERR_NCCL;
+    return SPMM_OK;
+}
+
+int issue_checked(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float* hC_rows, void* stream,
+                  bool join) {
+    if (!p) return SPMM_ERR_INVALID_ARG;
+    SPMM_TRY(check_plan_device(p));
+    SPMM_TRY(check_run_args(p, hA, hB, hC_rows));
+    DeviceState* st = nullptr;
+    SPMM_TRY(current_device_state(&st));
+    const int rc = run_issue(p, hA, hB, hC_rows, as_stream(stream), st, join);
+    if (rc != SPMM_OK) {
+        // Whatever was queued still reads the caller's host buffers: let it drain first (a
+        // collective that can no longer finish was aborted by the failing step).
+        for (cudaStream_t x : {p->s_in, p->s_comm, p->s_k, p->s_out}) cudaStreamSynchronize(x);
     }
-    return dev == p->device ? SPMM_OK : SPMM_ERR_INVALID_ARG;
+    return rc;
 }
 
 }  // namespace
@@ -547,6 +596,7 @@ int spmm_rank_plan_create(spmm_comm* comm, const spmm_csr_view* hA, int32_t N, v
         if (cudaStreamCreateWithFlags(x, cudaStreamNonBlocking) != cudaSuccess) return fail(SPMM_ERR_CUDA);
     p->b_pieces = p->world > 1 ? b_pieces_setting() : 1;
     p->ev.assign(4 + 2 * G + p->b_pieces, nullptr);
+    if (cudaEventCreateWithFlags(&p->kdone, cudaEventDisableTiming) != cudaSuccess) return fail(SPMM_ERR_CUDA);
     for (auto& e : p->ev)
         if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return fail(SPMM_ERR_CUDA);
     *out = p;
@@ -567,27 +617,22 @@ int spmm_rank_plan_info(const spmm_rank_plan* p, int32_t* row_begin, int32_t* ro
 }
 
 int spmm_rank_run(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float* hC_rows, void* stream) {
-    if (!p || !host_view_ok(hA)) return SPMM_ERR_INVALID_ARG;
-    SPMM_TRY(check_plan_device(p));
-    if (hA->rows != p->M || hA->cols != p->K || hA->nnz != p->nnz_all || hA->row_ptr[p->r0] != p->p0 ||
-        hA->row_ptr[p->r1] != p->p1)
-        return SPMM_ERR_INVALID_ARG;  // not the matrix the plan was made for
-    const size_t N = static_cast<size_t>(p->N);
-    if ((static_cast<size_t>(p->K) * N != 0 && !hB) || (static_cast<size_t>(p->rows()) * N != 0 && !hC_rows))
-        return SPMM_ERR_INVALID_ARG;
-    if (p->comm && p->comm->broken) return SPMM_ERR_NCCL;
-    DeviceState* st = nullptr;
-    SPMM_TRY(current_device_state(&st));
-    const cudaStream_t s = as_stream(stream);
     NvtxRange range("spmm_rank_run");
-    const int rc = run_issue(p, hA, hB, hC_rows, s, st);
-    if (rc != SPMM_OK) {
-        // Whatever was queued still reads the caller's host buffers: let it drain first (a
-        // collective that can no longer finish was aborted by the failing step).
-        for (cudaStream_t x : {p->s_in, p->s_comm, p->s_k, p->s_out}) cudaStreamSynchronize(x);
-        return rc;
-    }
-    return wait_event(p->ev.back(), p->comm, p->timeout_ms());
+    SPMM_TRY(issue_checked(p, hA, hB, hC_rows, stream, true));
+    return wait_event(p->end_event(), p->comm, p->timeout_ms());
+}
+
+int spmm_rank_submit(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float* hC_rows, void* stream) {
+    NvtxRange range("spmm_rank_submit");
+    return issue_checked(p, hA, hB, hC_rows, stream, false);
+}
+
+int spmm_rank_wait(spmm_rank_plan* p, void* stream) {
+    if (!p) return SPMM_ERR_INVALID_ARG;
+    SPMM_TRY(check_plan_device(p));
+    if (!p->submitted) return SPMM_OK;
+    SPMM_CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), p->end_event(), 0));
+    return wait_event(p->end_event(), p->comm, p->timeout_ms());
 }
 
 int spmm_rank_execute(spmm_rank_plan* p, void* stream) {

@@ -42,7 +42,8 @@ EXPORTS = [
     "spmm_csr_plan_create", "spmm_csr_plan_execute", "spmm_csr_plan_info", "spmm_csr_plan_destroy",
     "spmm_csr_plan_k_phases",
     "spmm_comm_unique_id", "spmm_comm_init", "spmm_comm_wrap", "spmm_comm_info", "spmm_comm_destroy",
-    "spmm_rank_plan_create", "spmm_rank_plan_info", "spmm_rank_run", "spmm_rank_execute", "spmm_rank_gather_b",
+    "spmm_rank_plan_create", "spmm_rank_plan_info", "spmm_rank_run", "spmm_rank_submit", "spmm_rank_wait",
+    "spmm_rank_execute", "spmm_rank_gather_b",
     "spmm_rank_plan_buffers", "spmm_rank_plan_destroy",
 ]
 
@@ -163,6 +164,8 @@ def lib() -> C.CDLL:
         "spmm_rank_plan_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32),
                                           C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]),
         "spmm_rank_run": (C.c_int, [vp, C.POINTER(CsrView), vp, vp, vp]),
+        "spmm_rank_submit": (C.c_int, [vp, C.POINTER(CsrView), vp, vp, vp]),
+        "spmm_rank_wait": (C.c_int, [vp, vp]),
         "spmm_rank_execute": (C.c_int, [vp, vp]),
         "spmm_rank_gather_b": (C.c_int, [vp, vp]),
         "spmm_rank_plan_buffers": (C.c_int, [vp, C.POINTER(vp), C.POINTER(vp)]),
@@ -603,6 +606,15 @@ class RankPlan:
     def run(self, A: HostCSR, B: np.ndarray, C_rows: np.ndarray, stream=None) -> None:
         v = A.view()
         check(lib().spmm_rank_run(self._h, C.byref(v), ptr(B), ptr(C_rows), stream_ptr(stream)), "spmm_rank_run")
+
+    def submit(self, A: HostCSR, B: np.ndarray, C_rows: np.ndarray, stream=None) -> None:
+        """run() without the wait; the arrays must stay alive and unchanged until wait()."""
+        v = A.view()
+        check(lib().spmm_rank_submit(self._h, C.byref(v), ptr(B), ptr(C_rows), stream_ptr(stream)),
+              "spmm_rank_submit")
+
+    def wait(self, stream=None) -> None:
+        check(lib().spmm_rank_wait(self._h, stream_ptr(stream)), "spmm_rank_wait")
 
     def execute(self, stream=None) -> None:
         check(lib().spmm_rank_execute(self._h, stream_ptr(stream)), "spmm_rank_execute")

@@ -86,6 +86,30 @@ def test_world_of_one_matches_oracle(cuda, case):
     plan.close()
 
 
+def test_submitted_runs_overlap_and_each_matches(cuda):
+    # Four runs submitted back to back (new B, new values of A, both), each into its own
+    # C, then one wait: every C must be its own product, bit for bit; then a synchronous run.
+    A, B = K.config("c2")
+    N = B.shape[1]
+    A2 = S.HostCSR(A.rows, A.cols, A.row_ptr, A.col_idx, (A.values * -0.5).astype(np.float32))
+    B2 = (B * 3.0).astype(np.float32)
+    plan = S.RankPlan(None, A, N)
+    jobs = [(A, B), (A, B2), (A2, B), (A2, B2)]
+    outs = [np.full((A.rows, N), np.nan, np.float32) for _ in jobs]
+    for (a, b), c in zip(jobs, outs):
+        plan.submit(a, b, c)
+    plan.wait()
+    for (a, b), c in zip(jobs, outs):
+        assert bits_equal(c, expected_rows(a, b, 0, a.rows, plan.algo))
+    C = np.full((A.rows, N), np.nan, np.float32)
+    plan.run(A, B2, C)
+    assert bits_equal(C, outs[1])
+    plan.wait()  # nothing left in flight: returns at once
+    code, detail = S.device_error(0)
+    assert code == 0, f"device error {code} at {detail}"
+    plan.close()
+
+
 def test_phased_plan_runs_pipelined_and_matches(cuda):
     # B of 128 MiB (131072 x 256, about the L2) and 4.3 GB of gathers: the plan takes 3 column
     # phases for the resident launches; the pipelined end-to-end run launches its row groups
@@ -162,6 +186,14 @@ _CHILD = textwrap.dedent("""
         plan.run(A, B, C)
     res.update(rows=(plan.row_begin, plan.row_end), share=(plan.b_row_begin, plan.b_row_end), algo=plan.algo,
                C=C[:plan.rows])
+    # Two runs submitted back to back (B, then 2 B), one wait.
+    C1 = np.full_like(C, np.nan)
+    C2 = np.full_like(C, np.nan)
+    B2 = (B * 2.0).astype(np.float32)
+    plan.submit(A, B, C1)
+    plan.submit(A, B2, C2)
+    plan.wait()
+    res.update(C1=C1[:plan.rows], C2=C2[:plan.rows])
     plan.gather_b()
     plan.execute()
     torch.cuda.synchronize()
@@ -200,7 +232,9 @@ def test_two_ranks_gather_b_and_return_their_rows(cuda, tmp_path, K_rows, pieces
     for r, d in enumerate(res):
         assert d["rows"] == (int(bounds[r]), int(bounds[r + 1]))
         assert d["share"] == (K_rows * r // 2, K_rows * (r + 1) // 2)
-        assert bits_equal(d["C"], expected_rows(A, B, *d["rows"], d["algo"]))
+        want = expected_rows(A, B, *d["rows"], d["algo"])
+        assert bits_equal(d["C"], want) and bits_equal(d["C1"], want)
+        assert bits_equal(d["C2"], expected_rows(A, (B * 2.0).astype(np.float32), *d["rows"], d["algo"]))
 
 
 def test_rank_that_never_joins_gives_timeout(cuda, tmp_path):
