@@ -422,16 +422,18 @@ int spmm_rank_submit(spmm_rank_plan* plan, const spmm_csr_view* hA, const float*
 int spmm_rank_wait(spmm_rank_plan* plan, void* stream);
 
 /* The kernels alone, on the device-resident operands the last spmm_rank_run left behind (the
- * rank's rows of A and the gathered B), into the plan's device C. Asynchronous, not collective.
- * After spmm_rank_submit, call spmm_rank_wait first. */
+ * rank's rows of A and the gathered B), into the plan's device C. Asynchronous, not collective;
+ * on the device it starts after the last run's copies back, whatever the stream. */
 int spmm_rank_execute(spmm_rank_plan* plan, void* stream);
 
 /* The all-gather of B alone (device to device over NVLink, from the shares already on every
- * rank's device). Collective, asynchronous on `stream`. */
+ * rank's device). Collective, asynchronous on `stream`, after the last run's copies back. */
 int spmm_rank_gather_b(spmm_rank_plan* plan, void* stream);
 
 /* The plan's device buffers: B (K x N, gathered) and the rank's rows of C. */
 int spmm_rank_plan_buffers(const spmm_rank_plan* plan, float** dB, float** dC);
+/* Waits for the plan's queued work (bounded: past the communicator's timeout it is aborted, so
+ * that a run waiting on a rank that is gone ends) and frees the plan. */
 void spmm_rank_plan_destroy(spmm_rank_plan* plan);
 
 /* Managed-memory single-GPU path: A, B, C in cudaMallocManaged memory, prefetched to the

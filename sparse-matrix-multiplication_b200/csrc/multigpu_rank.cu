@@ -171,13 +171,33 @@ struct spmm_rank_plan {
 namespace spmm_b200 {
 namespace {
 
+// Waits for everything queued on the plan's streams. Each wait is bounded by the plan's timeout:
+// a collective that waits on a rank that is gone is ended by aborting the communicator (NCCL's
+// kernels then leave), so the synchronisations that follow cannot wait for ever.
+int drain(spmm_rank_plan* p) {
+    int rc = SPMM_OK;
+    for (cudaStream_t x : {p->s_in, p->s_comm, p->s_k, p->s_out}) {
+        if (!x) continue;
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess) {
+            int r = cudaEventRecord(e, x) == cudaSuccess ? wait_event(e, p->comm, p->timeout_ms()) : SPMM_ERR_CUDA;
+            if (rc == SPMM_OK) rc = r;
+            cudaEventDestroy(e);
+        } else {
+            cudaGetLastError();
+        }
+    }
+    for (cudaStream_t x : {p->s_in, p->s_comm, p->s_k, p->s_out})
+        if (x) cudaStreamSynchronize(x);
+    return rc;
+}
+
 void release(spmm_rank_plan* p) {
     if (!p) return;
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(p->device);
-    for (cudaStream_t s : {p->s_in, p->s_comm, p->s_k, p->s_out})
-        if (s) cudaStreamSynchronize(s);
+    drain(p);
     if (p->cplan) spmm_csr_plan_destroy(p->cplan);
     for (cudaEvent_t e : p->ev)
         if (e) cudaEventDestroy(e);
@@ -421,11 +441,7 @@ int issue_checked(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, f
     DeviceState* st = nullptr;
     SPMM_TRY(current_device_state(&st));
     const int rc = run_issue(p, hA, hB, hC_rows, as_stream(stream), st, join);
-    if (rc != SPMM_OK) {
-        // Whatever was queued still reads the caller's host buffers: let it drain first (a
-        // collective that can no longer finish was aborted by the failing step).
-        for (cudaStream_t x : {p->s_in, p->s_comm, p->s_k, p->s_out}) cudaStreamSynchronize(x);
-    }
+    if (rc != SPMM_OK) drain(p);  // whatever was queued still reads the caller's host buffers
     return rc;
 }
 
@@ -638,6 +654,8 @@ int spmm_rank_wait(spmm_rank_plan* p, void* stream) {
 int spmm_rank_execute(spmm_rank_plan* p, void* stream) {
     if (!p) return SPMM_ERR_INVALID_ARG;
     SPMM_TRY(check_plan_device(p));
+    // On the device, after the last run's copies (it overwrites C, which they may still read).
+    if (p->submitted) SPMM_CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), p->end_event(), 0));
     return spmm_csr_plan_execute(p->cplan, p->d_B, p->d_C, stream);
 }
 
@@ -645,6 +663,7 @@ int spmm_rank_gather_b(spmm_rank_plan* p, void* stream) {
     if (!p) return SPMM_ERR_INVALID_ARG;
     SPMM_TRY(check_plan_device(p));
     if (p->comm && p->comm->broken) return SPMM_ERR_NCCL;
+    if (p->submitted) SPMM_CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), p->end_event(), 0));
     return gather_b_issue(p, as_stream(stream));
 }
 

@@ -110,6 +110,30 @@ def test_submitted_runs_overlap_and_each_matches(cuda):
     plan.close()
 
 
+def test_execute_after_submit_waits_on_the_device(cuda):
+    # A submitted run (new B) and, on another stream with no host wait between, the kernels
+    # alone: they start after the run's copies back, so the device C is the new product.
+    torch = cuda
+    A, B = K.config("c2")
+    N = B.shape[1]
+    plan = S.RankPlan(None, A, N)
+    C0 = np.full((A.rows, N), np.nan, np.float32)
+    plan.run(A, B, C0)
+    B2 = (B * 3.0).astype(np.float32)
+    want = expected_rows(A, B2, 0, A.rows, plan.algo)
+    C1 = np.full((A.rows, N), np.nan, np.float32)
+    plan.submit(A, B2, C1)
+    other = torch.cuda.Stream()
+    plan.execute(other)
+    other.synchronize()
+    plan.wait()
+    assert bits_equal(C1, want)
+    assert bits_equal(device_rows(torch, plan.d_C, A.rows, N), want)
+    code, detail = S.device_error(0)
+    assert code == 0, f"device error {code} at {detail}"
+    plan.close()
+
+
 def test_phased_plan_runs_pipelined_and_matches(cuda):
     # B of 128 MiB (131072 x 256, about the L2) and 4.3 GB of gathers: the plan takes 3 column
     # phases for the resident launches; the pipelined end-to-end run launches its row groups
