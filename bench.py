@@ -19,7 +19,9 @@ its 1/N share of B's rows in, the ranks all-gather B over NVLink, the kernels ru
 rows of C come back -- pipelined inside the library. Its `value` submits the steps back to back
 (spmm_rank_submit, one spmm_rank_wait at the end: a step's copy back overlaps the next step's
 copies in); `e2e.sync` times one synchronous spmm_rank_run per step. All are timed with CUDA
-events on the launching stream, max over ranks.
+events on the launching stream, max over ranks. `e2e.host_link` is the roofline of the end-to-end
+figure: each rank's bytes of a step moved as plain pinned copies, in and out at once, on all ranks
+together (`floor_ms`), and `frac` = floor_ms / ms_per_step.
 
 After the timed regions every rank checks its rows of C from the last end-to-end step against the
 CPU oracle (sampled rows, bit for bit) and the line carries `parity`.
@@ -277,6 +279,54 @@ def parity_rows(A, B: np.ndarray, r0: int, r1: int, C_rows: np.ndarray, algo: in
 # ------------------------------------------------------------------------ main
 
 
+def host_link(torch, h2d: int, d2h: int, R, reps: int = 5) -> dict:
+    """The host link's floor for one end-to-end step: `h2d` bytes in and `d2h` bytes out between
+    pinned host memory and this GPU, each direction alone and both at once (the in-copies in 16
+    pieces on one stream, the out-copies in 8 on another, as a step issues them), every rank at
+    the same time so that ranks sharing a PCIe switch or a host socket share it here too. Plain
+    copies, no kernels; median of `reps`, max over ranks."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    h_in = torch.empty(max(h2d, 1), dtype=torch.uint8).pin_memory()
+    h_out = torch.empty(max(d2h, 1), dtype=torch.uint8).pin_memory()
+    d_in = torch.empty(max(h2d, 1), dtype=torch.uint8, device=dev)
+    d_out = torch.empty(max(d2h, 1), dtype=torch.uint8, device=dev)
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    cur = torch.cuda.current_stream()
+
+    def issue(do_in: bool, do_out: bool):
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        for s, on, n, pieces, dst, src in ((s_in, do_in, h2d, 16, d_in, h_in), (s_out, do_out, d2h, 8, h_out, d_out)):
+            s.wait_event(ev)
+            if not on or n == 0:
+                continue
+            with torch.cuda.stream(s):
+                cut = [n * j // pieces for j in range(pieces + 1)]
+                for a, b in zip(cut, cut[1:]):
+                    dst[a:b].copy_(src[a:b], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(s)
+            cur.wait_event(done)
+
+    def timed(do_in: bool, do_out: bool) -> float:
+        ts = []
+        for _ in range(reps + 1):
+            R.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(cur)
+            issue(do_in, do_out)
+            b.record(cur)
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return R.max(statistics.median(ts[1:]))
+
+    t_in, t_out, t_both = timed(True, False), timed(False, True), timed(True, True)
+    del h_in, h_out, d_in, d_out
+    return {"h2d_gbs": round(h2d / (t_in * 1e-3) / 1e9, 2), "d2h_gbs": round(d2h / (t_out * 1e-3) / 1e9, 2),
+            "both_ms": round(t_both, 4)}
+
+
 class Ranks:
     """torch.distributed helpers: barrier, max / sum / min over ranks (no-ops at one rank)."""
 
@@ -463,15 +513,22 @@ def run_csr(args, torch, dist, R: Ranks, rank: int, world: int, local: int) -> d
         R.barrier()
         e2e_ms = R.max(t0.elapsed_time(t1) / ke)
         sync_ms = R.max(ms_sync_rank)
-        h2d = R.sum(float(4 * (rows_r + 1) + 8 * plan.nnz + 4 * (plan.b_row_end - plan.b_row_begin) * N))
-        d2h = R.sum(float(4 * rows_r * N))
+        h2d_rank = 4 * (rows_r + 1) + 8 * plan.nnz + 4 * (plan.b_row_end - plan.b_row_begin) * N
+        d2h_rank = 4 * rows_r * N
+        h2d, d2h = R.sum(float(h2d_rank)), R.sum(float(d2h_rank))
+        # The floor the host link sets: this rank's bytes of a step, in and out at once, on every
+        # rank together (after the timed region)
+        link = host_link(torch, h2d_rank, d2h_rank, R)
         e2e = {"value": round(total_flops / (e2e_ms * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "api": "spmm_rank_submit x steps + spmm_rank_wait (C ABI; per rank and step: its A rows and 1/N of "
                       "B's rows H2D from pinned buffers, NCCL all-gather of B over NVLink, kernels, its C rows D2H; "
                       "pipelined in row groups, consecutive steps overlapped)",
                "sync": {"value": round(total_flops / (sync_ms * 1e-3) / 1e9, 3), "ms_per_step": round(sync_ms, 4),
-                        "api": "spmm_rank_run per step (returns when the step's C is on the host)"}}
+                        "api": "spmm_rank_run per step (returns when the step's C is on the host)"},
+               "host_link": {**link, "floor_ms": link["both_ms"], "frac": round(link["both_ms"] / e2e_ms, 4),
+                             "probe": "each rank's step bytes as plain pinned copies, in and out at once, all ranks "
+                                      "together (in: 16 pieces, out: 8); frac = floor_ms / ms_per_step"}}
     else:
         plan.run(hA, hB, hC, stream)
     torch.cuda.synchronize()
