@@ -187,7 +187,10 @@ typedef struct spmm_csr_tuning {
     int32_t k_phases;
     int32_t schedule; /* merge-path chunk scheduling: 0 = auto (static), 1 = static: warp w takes
                          chunk w, 2 = dynamic: a resident grid takes chunks from a counter */
-    int32_t reserved[3];
+    int32_t phase_mode; /* column phases (k_phases > 1): 0 = auto, 1 = one launch per phase,
+                           2 = every phase in one launch (each warp takes its rows through the
+                           phases in order, one wave of resident warps); bit-identical */
+    int32_t reserved[2];
 } spmm_csr_tuning;
 
 /* C = A * B, FP32, on `stream`; A, B, C are device pointers. Asynchronous.
@@ -251,8 +254,11 @@ int spmm_csr_plan_create(const spmm_csr_view* A, int32_t N, const spmm_csr_tunin
                          spmm_csr_plan** plan);
 int spmm_csr_plan_execute(const spmm_csr_plan* plan, const float* B, float* C, void* stream);
 int spmm_csr_plan_info(const spmm_csr_plan* plan, int32_t* algo, int32_t* max_row, size_t* ws_bytes);
-/* Number of column phases the plan runs (kernel launches per spmm_csr_plan_execute). */
+/* Number of column phases the plan runs. */
 int spmm_csr_plan_k_phases(const spmm_csr_plan* plan, int32_t* k_phases);
+/* Kernel launches per spmm_csr_plan_execute: one per phase, or one for all of them
+ * (phase_mode 2), 0 for an empty product. */
+int spmm_csr_plan_launches(const spmm_csr_plan* plan, int32_t* launches);
 void spmm_csr_plan_destroy(spmm_csr_plan* plan);
 
 /* End-to-end call on HOST buffers: copies A and B to the current device (pinned or

@@ -75,8 +75,11 @@ struct CsrArgs {
     float* partials;     // num_chunks * 2 * N
     int b_policy;        // B loads: 0 plain, 1 L2 evict-last, 2 evict-last + no L1 allocation
     // Column phases (ROWWARP): launch `phase` of `phases` runs positions [split[phase-1][i],
-    // split[phase][i]) of row i (split[-1] = row start, split[phases-1] = row end).
+    // split[phase][i]) of row i (split[-1] = row start, split[phases-1] = row end). With
+    // phase_loop set, one launch runs every phase: each warp takes its rows through phase 0,
+    // then the same rows through phase 1, and so on.
     int phase, phases;
+    int phase_loop;
     int* ksplit;         // (phases - 1) x M split positions
     int* sched_counters; // dynamic merge schedule: [next chunk, warps done] per slab, zero between calls
     DeviceErrorRecord* err;
@@ -324,26 +327,40 @@ __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kerne
     const int nwarps = gridDim.x * kWarpsPerCta;
     const int col0 = blockIdx.y * W;
     const uint64_t pol = HINT ? evict_last_policy() : 0;
-    for (int i = warp; i < a.M; i += nwarps) {
-        int rs, re;
-        row_bounds(a, i, rs, re);
-        float acc[R][VEC];
-        float* crow = a.C + static_cast<size_t>(i) * a.N;
-        if constexpr (PHASED) {
-            // This phase's positions of row i; the chain continues from the value the
-            // previous phase stored in C (phase 0 starts from +0 and writes every row).
-            int lo = rs, hi = re;
-            if (a.phase > 0) lo = clampi(__ldcg(a.ksplit + static_cast<size_t>(a.phase - 1) * a.M + i), rs, re);
-            if (a.phase < a.phases - 1) hi = clampi(__ldcg(a.ksplit + static_cast<size_t>(a.phase) * a.M + i), lo, re);
-            if (a.phase > 0 && lo == hi) continue;
-            if (a.phase > 0) load_slab<VEC, R>(a, crow, col0, lane, acc);
-            else zero(acc);
-            accumulate<VEC, R, U, HINT>(a, ring, lo, hi, col0, lane, pol, acc);
-        } else {
+    if constexpr (PHASED) {
+        // Phase ph of row i: its positions [split[ph-1][i], split[ph][i]); the chain continues
+        // from the value phase ph-1 stored in C (phase 0 starts from +0 and writes every row).
+        // In one launch (phase_loop) a row's phases run on the same warp, lane for lane, in
+        // order: each lane reads back (ld.global.cg) only the C elements it stored itself.
+        const int ph0 = a.phase_loop ? 0 : a.phase;
+        const int ph1 = a.phase_loop ? a.phases : a.phase + 1;
+        for (int ph = ph0; ph < ph1; ++ph) {
+            const bool last = ph == a.phases - 1;
+            for (int i = warp; i < a.M; i += nwarps) {
+                int rs, re;
+                row_bounds(a, i, rs, re);
+                float acc[R][VEC];
+                float* crow = a.C + static_cast<size_t>(i) * a.N;
+                int lo = rs, hi = re;
+                if (ph > 0) lo = clampi(__ldcg(a.ksplit + static_cast<size_t>(ph - 1) * a.M + i), rs, re);
+                if (!last) hi = clampi(__ldcg(a.ksplit + static_cast<size_t>(ph) * a.M + i), lo, re);
+                if (ph > 0 && lo == hi) continue;
+                if (ph > 0) load_slab<VEC, R>(a, crow, col0, lane, acc);
+                else zero(acc);
+                accumulate<VEC, R, U, HINT>(a, ring, lo, hi, col0, lane, pol, acc);
+                // A partial that this launch reads back stays cached; the rest streams.
+                store_slab<VEC, R>(a, crow, col0, lane, acc, last || !a.phase_loop);
+            }
+        }
+    } else {
+        for (int i = warp; i < a.M; i += nwarps) {
+            int rs, re;
+            row_bounds(a, i, rs, re);
+            float acc[R][VEC];
             zero(acc);
             accumulate<VEC, R, U, HINT>(a, ring, rs, re, col0, lane, pol, acc);
+            store_slab<VEC, R>(a, a.C + static_cast<size_t>(i) * a.N, col0, lane, acc, true);
         }
-        store_slab<VEC, R>(a, crow, col0, lane, acc, true);
     }
 }
 
@@ -613,8 +630,12 @@ int check_tune(const spmm_csr_tuning* tune) {
     if (tune->b_policy < 0 || tune->b_policy > 2) return SPMM_ERR_INVALID_ARG;
     if (tune->k_phases < 0 || tune->k_phases > kMaxPhases) return SPMM_ERR_INVALID_ARG;
     if (tune->schedule < 0 || tune->schedule > 2) return SPMM_ERR_INVALID_ARG;
+    if (tune->phase_mode < 0 || tune->phase_mode > 2) return SPMM_ERR_INVALID_ARG;
     return SPMM_OK;
 }
+
+// Column phases in one launch (tune->phase_mode 2) or one launch per phase (0, 1).
+bool phase_in_one_launch(const spmm_csr_tuning* tune) { return tune && tune->phase_mode == 2; }
 
 int resolve_phases(int algo, const spmm_csr_tuning* tune) {
     return (algo == SPMM_CSR_ROWWARP && tune && tune->k_phases > 1) ? tune->k_phases : 1;
@@ -717,7 +738,8 @@ int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, 
         a.phases = resolve_phases(algo, tune);
         if (a.phases > 1) {
             // Column phases: split positions (computed here unless the caller holds them),
-            // then one launch per phase, then the workspace is cleared again.
+            // then one launch per phase (or one launch for all of them, on one wave of
+            // resident warps), then the workspace is cleared again.
             const size_t need = ksplit_bytes(a.phases, A->rows);
             if (need > ws_bytes || !ws) return SPMM_ERR_INVALID_ARG;
             a.ksplit = static_cast<int*>(ws);
@@ -725,9 +747,19 @@ int csr_f32_launch(const spmm_csr_view* A, const float* B, float* C, int32_t N, 
                 csr_ksplit_kernel<<<grid.x, kThreads, 0, stream>>>(a);
                 SPMM_CUDA_TRY(cudaGetLastError());
             }
-            for (a.phase = 0; a.phase < a.phases; ++a.phase) {
-                launch(g, algo, a, grid, stream);
+            if (phase_in_one_launch(tune)) {
+                const long long resident = static_cast<long long>(st->sm_count) * SPMM_CSR_MIN_CTAS * kWarpsPerCta;
+                const long long warps1 = std::min<long long>(A->rows, resident);
+                dim3 grid1(static_cast<unsigned>((warps1 + kWarpsPerCta - 1) / kWarpsPerCta), grid.y, 1);
+                a.phase_loop = 1;
+                a.phase = 0;
+                launch(g, algo, a, grid1, stream);
                 SPMM_CUDA_TRY(cudaGetLastError());
+            } else {
+                for (a.phase = 0; a.phase < a.phases; ++a.phase) {
+                    launch(g, algo, a, grid, stream);
+                    SPMM_CUDA_TRY(cudaGetLastError());
+                }
             }
             if (!ksplit_ready) SPMM_CUDA_TRY(cudaMemsetAsync(ws, 0, need, stream));
             return SPMM_OK;

@@ -148,7 +148,7 @@ struct spmm_rank_plan {
     spmm_csr_view dview{};
     spmm_csr_plan* cplan = nullptr;
     int32_t algo = SPMM_CSR_ROWWARP;
-    int32_t k_phases = 1;
+    int32_t launches = 1;  // kernel launches of one spmm_rank_execute
     int32_t b_pieces = 1;  // pieces of the B share copied and exchanged one after another
     bool pipelined = false;
     cudaStream_t s_in = nullptr, s_comm = nullptr, s_k = nullptr, s_out = nullptr;
@@ -589,7 +589,7 @@ int spmm_rank_plan_create(spmm_comm* comm, const spmm_csr_view* hA, int32_t N, v
     rc = spmm_csr_plan_create(&p->dview, N, nullptr, stream, &p->cplan);
     if (rc != SPMM_OK) return fail(rc);
     spmm_csr_plan_info(p->cplan, &p->algo, nullptr, nullptr);
-    spmm_csr_plan_k_phases(p->cplan, &p->k_phases);
+    spmm_csr_plan_launches(p->cplan, &p->launches);
     // Row groups: ROWWARP computes every row on its own, so any grouping of the rows into
     // launches gives the same bits, with or without the plan's column phases (each element's
     // chain is the same however its positions are cut); the pipelined run launches each group
@@ -628,7 +628,7 @@ int spmm_rank_plan_info(const spmm_rank_plan* p, int32_t* row_begin, int32_t* ro
     if (b_row_begin) *b_row_begin = p->b_bounds[p->rank];
     if (b_row_end) *b_row_end = p->b_bounds[p->rank + 1];
     if (algo) *algo = p->algo;
-    if (launches) *launches = p->rows() > 0 && p->N > 0 ? p->k_phases : 0;
+    if (launches) *launches = p->launches;
     return SPMM_OK;
 }
 

@@ -142,6 +142,17 @@ int spmm_csr_plan_k_phases(const spmm_csr_plan* p, int32_t* k_phases) {
     return SPMM_OK;
 }
 
+int spmm_csr_plan_launches(const spmm_csr_plan* p, int32_t* launches) {
+    if (!p || !launches) return SPMM_ERR_INVALID_ARG;
+    if (p->A.rows == 0 || p->N == 0) {
+        *launches = 0;
+        return SPMM_OK;
+    }
+    const bool phased = p->algo == SPMM_CSR_ROWWARP && p->tune.k_phases > 1;
+    *launches = phased && p->tune.phase_mode != 2 ? p->tune.k_phases : 1;
+    return SPMM_OK;
+}
+
 int spmm_csr_plan_info(const spmm_csr_plan* p, int32_t* algo, int32_t* max_row, size_t* ws_bytes) {
     if (!p) return SPMM_ERR_INVALID_ARG;
     if (algo) *algo = p->algo;

@@ -40,7 +40,7 @@ EXPORTS = [
     "spmm_bsr16_plan_destroy",
     "spmm_csr_f32_noalloc", "spmm_csr_to_bsr16_device_count", "spmm_csr_to_bsr16_device_fill",
     "spmm_csr_plan_create", "spmm_csr_plan_execute", "spmm_csr_plan_info", "spmm_csr_plan_destroy",
-    "spmm_csr_plan_k_phases",
+    "spmm_csr_plan_k_phases", "spmm_csr_plan_launches",
     "spmm_comm_unique_id", "spmm_comm_init", "spmm_comm_wrap", "spmm_comm_info", "spmm_comm_destroy",
     "spmm_rank_plan_create", "spmm_rank_plan_info", "spmm_rank_run", "spmm_rank_submit", "spmm_rank_wait",
     "spmm_rank_execute", "spmm_rank_gather_b",
@@ -84,7 +84,7 @@ class BsrStats(C.Structure):
 
 class CsrTuning(C.Structure):
     _fields_ = [("chunk", C.c_int32), ("col_pass", C.c_int32), ("b_policy", C.c_int32), ("k_phases", C.c_int32),
-                ("schedule", C.c_int32), ("reserved", C.c_int32 * 3)]
+                ("schedule", C.c_int32), ("phase_mode", C.c_int32), ("reserved", C.c_int32 * 2)]
 
 
 class HybridPlan(C.Structure):
@@ -154,6 +154,7 @@ def lib() -> C.CDLL:
         "spmm_csr_plan_execute": (C.c_int, [vp, vp, vp, vp]),
         "spmm_csr_plan_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_size_t)]),
         "spmm_csr_plan_k_phases": (C.c_int, [vp, C.POINTER(i32)]),
+        "spmm_csr_plan_launches": (C.c_int, [vp, C.POINTER(i32)]),
         "spmm_csr_plan_destroy": (None, [vp]),
         "spmm_comm_unique_id": (C.c_int, [vp]),
         "spmm_comm_init": (C.c_int, [vp, i32, i32, i32, C.POINTER(vp)]),
@@ -449,7 +450,9 @@ class CsrPlan:
         self.algo, self.max_row, self.ws_bytes = int(algo.value), int(mx.value), int(ws.value)
         ph = C.c_int32()
         check(lib().spmm_csr_plan_k_phases(h, C.byref(ph)), "spmm_csr_plan_k_phases")
-        self.k_phases = int(ph.value)  # kernel launches per execute
+        self.k_phases = int(ph.value)  # column phases
+        check(lib().spmm_csr_plan_launches(h, C.byref(ph)), "spmm_csr_plan_launches")
+        self.launches = int(ph.value)  # kernel launches per execute
 
     def execute(self, B, Cout, stream=None) -> None:
         check(lib().spmm_csr_plan_execute(self._h, ptr(B), ptr(Cout), stream_ptr(stream)), "spmm_csr_plan_execute")

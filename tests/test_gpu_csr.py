@@ -287,19 +287,21 @@ def test_b_load_policies_bit_exact(cuda, policy, algo):
     assert_parity(run(cuda, A, B, algo, tuning=t), A, B, algo, tuning=t)
 
 
+@pytest.mark.parametrize("mode", [1, 2])
 @pytest.mark.parametrize("phases", [2, 3, 5, 8])
 @pytest.mark.parametrize("N", [64, 100, 257])
-def test_column_phases_bit_exact(cuda, phases, N):
-    # ROWWARP in column phases: each launch continues every element's chain from C, so the
-    # result is the one sequential chain; empty phases, rows empty in every phase and N > 256
-    # (two slabs per phase) included. The workspace is all-zero again afterwards.
+def test_column_phases_bit_exact(cuda, phases, N, mode):
+    # ROWWARP in column phases, one launch per phase (mode 1) or every phase in one launch
+    # (mode 2): each phase continues every element's chain from C, so the result is the one
+    # sequential chain; empty phases, rows empty in every phase and N > 256 (two slabs per
+    # phase) included. The workspace is all-zero again afterwards.
     rng = np.random.default_rng(phases * 1000 + N)
     lens = rng.integers(0, 60, size=900)
     lens[::50] = 0
     lens[7] = 700
     A = K.random_csr(900, 3000, lens, seed=N)
     B = K.dense(3000, N, phases)
-    t = S.CsrTuning(k_phases=phases)
+    t = S.CsrTuning(k_phases=phases, phase_mode=mode)
     torch = cuda
     rp, ci, v = _dev(torch, A.row_ptr), _dev(torch, A.col_idx), _dev(torch, A.values)
     view = S.device_view(A.rows, A.cols, rp, ci, v)
@@ -328,17 +330,21 @@ def test_column_phases_unsorted_rows_keep_stored_order(cuda):
             ci[s + 1] = ci[s]
     U = S.HostCSR(A.rows, A.cols, A.row_ptr.copy(), ci, A.values.copy())
     B = K.dense(2000, 128, 6)
-    assert_parity(run(cuda, U, B, S.CSR_ROWWARP, tuning=S.CsrTuning(k_phases=4)), U, B, S.CSR_ROWWARP)
+    for mode in (1, 2):
+        t = S.CsrTuning(k_phases=4, phase_mode=mode)
+        assert_parity(run(cuda, U, B, S.CSR_ROWWARP, tuning=t), U, B, S.CSR_ROWWARP)
 
 
-def test_plan_with_column_phases(cuda):
+@pytest.mark.parametrize("mode", [0, 2])
+def test_plan_with_column_phases(cuda, mode):
     torch = cuda
     A, B = K.config("c1")
     N = B.shape[1]
     rp, ci, v = _dev(torch, A.row_ptr), _dev(torch, A.col_idx), _dev(torch, A.values)
     view = S.device_view(A.rows, A.cols, rp, ci, v)
-    plan = S.CsrPlan(view, N, tuning=S.CsrTuning(k_phases=3), stream=torch.cuda.current_stream())
+    plan = S.CsrPlan(view, N, tuning=S.CsrTuning(k_phases=3, phase_mode=mode), stream=torch.cuda.current_stream())
     assert plan.algo == S.CSR_ROWWARP and plan.k_phases == 3
+    assert plan.launches == (1 if mode == 2 else 3)
     Bd = _dev(torch, B)
     for _ in range(3):  # the plan keeps its split positions across executions
         Cd = torch.full((A.rows, N), float("nan"), device="cuda")
@@ -346,9 +352,10 @@ def test_plan_with_column_phases(cuda):
         torch.cuda.synchronize()
         assert_parity(Cd.cpu().numpy(), A, B, S.CSR_ROWWARP)
     plan.close()
-    for bad in (-1, 9):
+    for bad in ({"k_phases": -1}, {"k_phases": 9}, {"k_phases": 3, "phase_mode": 3},
+                {"k_phases": 3, "phase_mode": -1}):
         with pytest.raises(S.SpmmError) as e:
-            S.csr_workspace_size(view, N, S.CSR_ROWWARP, S.CsrTuning(k_phases=bad))
+            S.csr_workspace_size(view, N, S.CSR_ROWWARP, S.CsrTuning(**bad))
         assert e.value.status == -1
 
 
