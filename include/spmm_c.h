@@ -293,6 +293,10 @@ int spmm_bsr16_plan_execute(const spmm_bsr_plan* plan, const void* B16, float* C
  * schedule bytes (0 = no schedule). */
 int spmm_bsr16_plan_info(const spmm_bsr_plan* plan, int32_t* group, int32_t* max_steps,
                          size_t* schedule_bytes);
+/* Block stride of the plan's grouped A copies (0: one copy per block). With stride S, a step whose
+ * G blocks sit at p, p + S, ..., p + (G-1) S in the value array (block-diagonal, evenly filled
+ * bands) loads them in one TMA copy instead of G. */
+int spmm_bsr16_plan_a_stride(const spmm_bsr_plan* plan, int32_t* a_stride);
 void spmm_bsr16_plan_destroy(spmm_bsr_plan* plan);
 
 /* BSR-16 path variants for measurement: 0 = auto, 1 = tcgen05, 2 = CUDA-core fallback. */

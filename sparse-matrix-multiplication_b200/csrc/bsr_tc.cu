@@ -40,6 +40,7 @@
 #include <cstdint>
 #include <mutex>
 #include <new>
+#include <vector>
 
 #include "common.cuh"
 
@@ -56,6 +57,9 @@ struct spmm_bsr_plan {
     int32_t device = 0;
     bool tc = false;
     CUtensorMap ta{};
+    CUtensorMap ta4{};     // A's blocks in groups of a_stride (grouped copies), if a_stride > 0
+    int32_t a_stride = 0;
+    int32_t a_groups = 0;
     // B's tensor map for the last B16 pointer executed (re-encoded only when B16 changes: the
     // encode is host work between the caller's launch and the kernel's start).
     mutable std::mutex tb_mu;
@@ -88,6 +92,12 @@ struct BsrArgs {
     // [steps, rows_mask, then per step: block column, row mask, G block indices].
     const int* __restrict__ sched;
     int sched_stride;
+    // Grouped A loads (plans): when a stage's G blocks sit at p, p + S, ..., p + (G-1) S in the
+    // value array (S = a_stride > 0; the same S for every block-row step of a block-diagonal
+    // or evenly filled band), one 4-D copy of A's blocks viewed as [a_groups][S][16][16]
+    // fetches all G of them. 0: one copy per block.
+    int a_stride;
+    int a_groups;
 };
 
 template <int G>
@@ -193,6 +203,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z,
+                                            int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -252,7 +270,8 @@ __device__ __forceinline__ uint32_t instr_desc(int dtype, uint32_t n) {
 
 template <int G, bool SCHED>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    bsr_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_a, BsrArgs a) {
+    bsr_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_a,
+                       const __grid_constant__ CUtensorMap tmap_a4, BsrArgs a) {
     using L = Layout<G>;
     extern __shared__ uint8_t smem_raw[];
     // 1 KB alignment (SW128 atoms) in the shared address space.
@@ -318,6 +337,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+            if (a.a_stride > 0)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a4)) : "memory");
         }
         int cur = 0, end = 0;
         if (!SCHED && lane < G) {
@@ -391,10 +412,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     // one 16 x 16 box (32-byte swizzle, K-major as the MMA reads it).
                     tma_load_2d(stage, &tmap_b, full0 + 8 * sl, n0, sched_bc[lane] * 16);
                     tma_load_2d(stage + 2048, &tmap_b, full0 + 8 * sl, n0 + 64, sched_bc[lane] * 16);
-                    for (unsigned m = mask; m; m &= m - 1) {
-                        const int j = __ffs(m) - 1;
-                        tma_load_2d(stage + L::kBTile + j * L::kASlot, &tmap_a, full0 + 8 * sl, 0,
-                                    sched_blk[lane * G + j] * 16);
+                    // A's blocks: one grouped copy when they are S apart in the value array (and
+                    // the group lies inside the grouped view), else one copy per block.
+                    const int p0 = sched_blk[lane * G];
+                    bool grouped = a.a_stride > 0 && mask == (1u << G) - 1u && p0 >= 0 &&
+                                   p0 / a.a_stride + G - 1 < a.a_groups;
+#pragma unroll
+                    for (int j = 1; j < G; ++j) grouped = grouped && sched_blk[lane * G + j] == p0 + j * a.a_stride;
+                    if (grouped) {
+                        tma_load_4d(stage + L::kBTile, &tmap_a4, full0 + 8 * sl, 0, 0, p0 % a.a_stride,
+                                    p0 / a.a_stride);
+                    } else {
+                        for (unsigned m = mask; m; m &= m - 1) {
+                            const int j = __ffs(m) - 1;
+                            tma_load_2d(stage + L::kBTile + j * L::kASlot, &tmap_a, full0 + 8 * sl, 0,
+                                        sched_blk[lane * G + j] * 16);
+                        }
                     }
                 }
             }
@@ -609,8 +642,58 @@ int encode_a_map(CUtensorMap* ta, const BsrArgs& a) {
     return encode_2d(ta, a.values, 16, static_cast<uint64_t>(a.num_blocks) * 16, 32, 16, 16, CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
+// A's blocks as [num_blocks / S][S][16][16] (blocks past the last whole group left out): a box of
+// {16, 16, 1, G} at (0, 0, p % S, p / S) is blocks p, p + S, ..., p + (G-1) S, landing as G
+// consecutive 512-byte SW32 slots, the layout of G single-block copies.
+int encode_a_group_map(CUtensorMap* map, const BsrArgs& a, int S, int G) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return SPMM_ERR_UNSUPPORTED;
+    const cuuint64_t dims[4] = {16, 16, static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(a.num_blocks / S)};
+    const cuuint64_t strides[3] = {32, 512, 512ull * static_cast<cuuint64_t>(S)};
+    const cuuint32_t box[4] = {16, 16, 1, static_cast<cuuint32_t>(G)};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<uint16_t*>(a.values), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? SPMM_OK : SPMM_ERR_INVALID_ARG;
+}
+
+// The block stride S of the grouped A copies: the most common distance between the blocks of
+// consecutive block-rows in the schedule's full steps (every row of the group present and the
+// blocks evenly spaced), over the first `ints` entries of a schedule copied to the host. 0 when
+// no full step is evenly spaced. Any S is safe: the kernel checks every stage against it.
+int pick_a_stride(const std::vector<int>& sched, int stride, int groups, int G) {
+    std::vector<std::pair<int, int>> counts;  // (S, steps)
+    const unsigned all = (1u << G) - 1u;
+    for (int g = 0; g < groups; ++g) {
+        const size_t rec = static_cast<size_t>(g) * stride;
+        if (rec + 2 > sched.size()) break;
+        const int steps = sched[rec];
+        for (int t = 0; t < steps; ++t) {
+            const size_t e = rec + 2 + static_cast<size_t>(t) * (2 + G);
+            if (e + 2 + G > sched.size()) break;
+            if (static_cast<unsigned>(sched[e + 1]) != all) continue;
+            const int d = sched[e + 3] - sched[e + 2];
+            bool even = d > 0;
+            for (int j = 2; j < G && even; ++j) even = sched[e + 2 + j] - sched[e + 2 + j - 1] == d;
+            if (!even) continue;
+            auto it = std::find_if(counts.begin(), counts.end(), [d](const std::pair<int, int>& c) { return c.first == d; });
+            if (it == counts.end()) {
+                if (counts.size() < 64) counts.emplace_back(d, 1);
+            } else {
+                ++it->second;
+            }
+        }
+    }
+    int best = 0, best_n = 0;
+    for (const auto& c : counts)
+        if (c.second > best_n) best = c.first, best_n = c.second;
+    return best;
+}
+
 template <int G, bool SCHED>
-int launch_tc_maps(const BsrArgs& a, const CUtensorMap& tb, const CUtensorMap& ta, cudaStream_t s) {
+int launch_tc_maps(const BsrArgs& a, const CUtensorMap& tb, const CUtensorMap& ta, const CUtensorMap& ta4,
+                   cudaStream_t s) {
     using L = Layout<G>;
     // The shared-memory attribute belongs to the current device's context: set it once per
     // device (a bit per device id), not on every launch.
@@ -624,7 +707,7 @@ int launch_tc_maps(const BsrArgs& a, const CUtensorMap& tb, const CUtensorMap& t
         attr_set.fetch_or(bit, std::memory_order_acq_rel);
     }
     const dim3 grid((a.block_rows + G - 1) / G, (a.N + 127) / 128);
-    bsr_tcgen05_kernel<G, SCHED><<<grid, kTcThreads, L::kDynamic, s>>>(tb, ta, a);
+    bsr_tcgen05_kernel<G, SCHED><<<grid, kTcThreads, L::kDynamic, s>>>(tb, ta, ta4, a);
     SPMM_CUDA_TRY(cudaGetLastError());
     return SPMM_OK;
 }
@@ -634,7 +717,7 @@ int launch_tc(const BsrArgs& a, cudaStream_t s) {
     CUtensorMap tb, ta;
     SPMM_TRY(encode_b_map(&tb, a));
     SPMM_TRY(encode_a_map(&ta, a));
-    return launch_tc_maps<G, false>(a, tb, ta, s);
+    return launch_tc_maps<G, false>(a, tb, ta, ta, s);  // a.a_stride == 0: no grouped copies
 }
 
 // Plans: the producer's merge of G block-column lists, done once for every CTA group and
@@ -815,6 +898,20 @@ int spmm_bsr16_plan_create(const spmm_bsr_view* A, int32_t N, void* stream, spmm
                 }
             }
         }
+        // Grouped A copies: the block stride from (at most 1 MiB of) the schedule.
+        if (rc == SPMM_OK && p->sched) {
+            const size_t ints = std::min<size_t>(p->sched_bytes / sizeof(int), (1u << 20) / sizeof(int));
+            std::vector<int> host(ints);
+            if (cudaMemcpy(host.data(), p->sched, ints * sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+                rc = SPMM_ERR_CUDA;
+            } else {
+                const int S = pick_a_stride(host, p->stride, groups, p->group);
+                if (S > 0 && A->num_blocks / S >= p->group && encode_a_group_map(&p->ta4, a, S, p->group) == SPMM_OK) {
+                    p->a_stride = S;
+                    p->a_groups = A->num_blocks / S;
+                }
+            }
+        }
     }
     if (rc != SPMM_OK) {
         cudaFree(p->sched);
@@ -849,6 +946,8 @@ int spmm_bsr16_plan_execute(const spmm_bsr_plan* p, const void* B16, float* C, v
     a.err = st->err;
     a.sched = p->sched;
     a.sched_stride = p->stride;
+    a.a_stride = p->a_stride;
+    a.a_groups = p->a_groups;
     CUtensorMap tb;
     {
         std::lock_guard<std::mutex> lock(p->tb_mu);
@@ -858,8 +957,9 @@ int spmm_bsr16_plan_execute(const spmm_bsr_plan* p, const void* B16, float* C, v
         }
         tb = p->tb;
     }
-    if (p->group == 8) return launch_tc_maps<8, true>(a, tb, p->ta, s);
-    return launch_tc_maps<4, true>(a, tb, p->ta, s);
+    const CUtensorMap& ta4 = p->a_stride > 0 ? p->ta4 : p->ta;
+    if (p->group == 8) return launch_tc_maps<8, true>(a, tb, p->ta, ta4, s);
+    return launch_tc_maps<4, true>(a, tb, p->ta, ta4, s);
 }
 
 int spmm_bsr16_plan_info(const spmm_bsr_plan* p, int32_t* group, int32_t* max_steps, size_t* schedule_bytes) {
@@ -867,6 +967,12 @@ int spmm_bsr16_plan_info(const spmm_bsr_plan* p, int32_t* group, int32_t* max_st
     if (group) *group = p->tc ? p->group : 0;
     if (max_steps) *max_steps = p->max_steps;
     if (schedule_bytes) *schedule_bytes = p->sched_bytes;
+    return SPMM_OK;
+}
+
+int spmm_bsr16_plan_a_stride(const spmm_bsr_plan* p, int32_t* a_stride) {
+    if (!p || !a_stride) return SPMM_ERR_INVALID_ARG;
+    *a_stride = p->a_stride;
     return SPMM_OK;
 }
 

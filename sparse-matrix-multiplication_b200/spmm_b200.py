@@ -37,7 +37,7 @@ EXPORTS = [
     "spmm_bsr16_algo", "spmm_device_error", "spmm_hybrid_default_threshold", "spmm_hybrid_choose",
     "spmm_backend_name", "spmm_hybrid_run", "spmm_gpu_count", "spmm_multigpu_run", "spmm_unified_run",
     "spmm_unified_run_ex", "spmm_bsr16_plan_create", "spmm_bsr16_plan_execute", "spmm_bsr16_plan_info",
-    "spmm_bsr16_plan_destroy",
+    "spmm_bsr16_plan_destroy", "spmm_bsr16_plan_a_stride",
     "spmm_csr_f32_noalloc", "spmm_csr_to_bsr16_device_count", "spmm_csr_to_bsr16_device_fill",
     "spmm_csr_plan_create", "spmm_csr_plan_execute", "spmm_csr_plan_info", "spmm_csr_plan_destroy",
     "spmm_csr_plan_k_phases", "spmm_csr_plan_launches",
@@ -135,6 +135,7 @@ def lib() -> C.CDLL:
         "spmm_bsr16_plan_execute": (C.c_int, [vp, vp, vp, vp]),
         "spmm_bsr16_plan_info": (C.c_int, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_size_t)]),
         "spmm_bsr16_plan_destroy": (None, [vp]),
+        "spmm_bsr16_plan_a_stride": (C.c_int, [vp, C.POINTER(i32)]),
         "spmm_device_error": (C.c_int, [i32, C.POINTER(i32), C.POINTER(i64), i32]),
         "spmm_hybrid_default_threshold": (f32, []),
         "spmm_hybrid_choose": (C.c_int, [C.POINTER(CsrView), i32, f32, C.POINTER(HybridPlan)]),
@@ -419,6 +420,9 @@ class BsrPlan:
         g, ms, nb = C.c_int32(), C.c_int32(), C.c_size_t()
         check(lib().spmm_bsr16_plan_info(h, C.byref(g), C.byref(ms), C.byref(nb)), "spmm_bsr16_plan_info")
         self.group, self.max_steps, self.schedule_bytes = int(g.value), int(ms.value), int(nb.value)
+        st = C.c_int32()
+        check(lib().spmm_bsr16_plan_a_stride(h, C.byref(st)), "spmm_bsr16_plan_a_stride")
+        self.a_stride = int(st.value)  # block stride of the grouped A copies (0: none)
 
     def execute(self, B16, Cout, stream=None) -> None:
         check(lib().spmm_bsr16_plan_execute(self._h, ptr(B16), ptr(Cout), stream_ptr(stream)), "spmm_bsr16_plan_execute")

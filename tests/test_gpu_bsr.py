@@ -147,18 +147,40 @@ def _plan_run(torch, Hb: S.HostBSR, B16: np.ndarray, N: int):
         outs.append(Cd.cpu().numpy())
     code, detail = S.device_error(0)
     assert code == 0, f"device error {code} ({detail})"
-    info = (plan.group, plan.max_steps, plan.schedule_bytes)
+    info = (plan.group, plan.max_steps, plan.schedule_bytes, plan.a_stride)
     plan.close()
     return outs, info
 
 
-@pytest.mark.parametrize("case", ["c3", "c3_bf16", "banded", "ragged_g8", "empty_groups", "n_tail"])
+def _block_diagonal_with_extras(n: int, blk: int, extra_rows, seed: int) -> S.HostCSR:
+    """Dense blk x blk diagonal blocks; each row in extra_rows also gets one nonzero three blocks
+    to the right (another BSR block in its block-row)."""
+    rng = np.random.default_rng(seed)
+    row_ptr, cols = [0], []
+    for i in range(n):
+        d = i // blk
+        c = list(range(d * blk, min((d + 1) * blk, n)))
+        if i in extra_rows:
+            c = sorted(set(c) | {(d * blk + 3 * blk + 5) % n})
+        cols.extend(c)
+        row_ptr.append(len(cols))
+    vals = rng.uniform(-1, 1, size=len(cols)).astype(np.float32)
+    return S.HostCSR(n, n, np.array(row_ptr, np.int32), np.array(cols, np.int32), vals)
+
+
+@pytest.mark.parametrize("case", ["c3", "c3_bf16", "banded", "ragged_g8", "empty_groups", "n_tail", "diag_mixed"])
 def test_plan_schedule_matches_per_call(cuda, case):
-    # The precomputed per-CTA schedule gives the per-call kernel's result bit for bit.
+    # The precomputed per-CTA schedule gives the per-call kernel's result bit for bit, with
+    # the grouped A copies where a step's blocks are evenly spaced and single-block copies
+    # where they are not (diag_mixed: extra blocks shift and unbalance some block-rows, and
+    # the last group of the grouped view is partial).
     dtype = S.DTYPE_BF16 if case == "c3_bf16" else S.DTYPE_F16
     if case.startswith("c3"):
         A, Bf = K.config("c3")
         N = 256
+    elif case == "diag_mixed":
+        A = _block_diagonal_with_extras(2048, 128, {5, 700, 1500}, seed=8)
+        Bf, N = K.dense(2048, 256, 3), 256
     elif case == "banded":
         A, Bf = K.config("c2")
         N = 128
@@ -177,8 +199,11 @@ def test_plan_schedule_matches_per_call(cuda, case):
         Bf, N = K.dense(999, 136, 2), 136
     Hb = S.csr_to_bsr16(A, dtype)
     B16 = O.to_half_bits(Bf, bf16=dtype == S.DTYPE_BF16)
-    (c0, c1), (group, steps, nbytes) = _plan_run(cuda, Hb, B16, N)
+    (c0, c1), (group, steps, nbytes, a_stride) = _plan_run(cuda, Hb, B16, N)
     assert group in (4, 8) and steps > 0 and nbytes > 0
+    if case.startswith("c3") or case == "diag_mixed":
+        assert a_stride == 8  # 8 blocks per block-row: a step's 4 blocks are 8 apart
+        assert Hb.num_blocks == (1024 if case == "diag_mixed" else 4096) + (3 if case == "diag_mixed" else 0)
     want = run_bsr(cuda, Hb, B16, N, algo=1)
     assert np.array_equal(c0.view(np.uint32), want.view(np.uint32))
     assert np.array_equal(c1.view(np.uint32), want.view(np.uint32))
@@ -189,6 +214,6 @@ def test_plan_falls_back_off_the_tensor_core_path(cuda):
     A = K.random_csr(64, 64, np.full(64, 8), seed=1)
     Hb = S.csr_to_bsr16(A)
     B16 = O.to_half_bits(K.dense(64, 20, 2))
-    (c0, _), (group, _, nbytes) = _plan_run(cuda, Hb, B16, 20)  # N % 8 != 0: CUDA-core kernel
+    (c0, _), (group, _, nbytes, _) = _plan_run(cuda, Hb, B16, 20)  # N % 8 != 0: CUDA-core kernel
     assert group == 0 and nbytes == 0
     check_bsr(c0, Hb, B16, S.DTYPE_F16)
