@@ -28,7 +28,8 @@ CPU oracle (sampled rows, bit for bit) and the line carries `parity`.
 
 `roofline` carries the HBM fraction of the compulsory bytes (the reference's roofline model)
 and, for the CSR kernels, `gather_ceiling`: the rate at which the kernel pulls B rows into the
-SMs against a load-only probe of random 1 KB row fetches from an L2-resident part of B.
+SMs against a load-only probe of random row fetches of B's width (N = 256 or 128) from an
+L2-resident part of B.
 
 `--rank-slice R/G` runs rank R's rows of a G-way split alone on one GPU (the same kernel launch
 that rank runs at G GPUs), to profile a rank's launch with ncu on a single GPU.
@@ -195,33 +196,34 @@ class Clocks:
 
 def gather_ceiling(torch, b_ptr: int, n_cols: int, rows: int, fetches: int, stream) -> float | None:
     """Random whole-row gather rate (GB/s) of this GPU over the first `rows` rows of the device B
-    at b_ptr (N = 256 only): lib/libspmm_probe.so, same residency and load width as the CSR
-    kernels, no arithmetic. The median of 5 launches of `fetches` 1 KB rows each."""
+    at b_ptr (N = 256 or 128: 1 KB or 512-byte rows): lib/libspmm_probe.so, same residency and
+    load width as the CSR kernels, no arithmetic. The median of 5 launches of `fetches` rows."""
     import ctypes as C
 
     so = PKG / "lib" / "libspmm_probe.so"
-    if n_cols != 256 or not so.exists() or fetches < 4:
+    if n_cols not in (128, 256) or not so.exists() or fetches < 8:
         return None
     lib = C.CDLL(str(so))
-    lib.spmm_probe_gather.argtypes = [C.c_void_p, C.c_uint32, C.c_longlong, C.c_uint32, C.c_void_p, C.c_void_p]
+    lib.spmm_probe_gather_rows.argtypes = [C.c_void_p, C.c_int, C.c_uint32, C.c_longlong, C.c_uint32, C.c_void_p,
+                                           C.c_void_p]
     ctas = C.c_int()
     if lib.spmm_probe_ctas(C.byref(ctas)) != 0:
         return None
     out = torch.empty(ctas.value * 256, dtype=torch.float32, device="cuda")
-    fetches -= fetches % 4
+    fetches -= fetches % 8
     ts = []
     for i in range(7):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        rc = lib.spmm_probe_gather(C.c_void_p(b_ptr), rows, fetches, i, C.c_void_p(out.data_ptr()),
-                                   C.c_void_p(stream.cuda_stream))
+        rc = lib.spmm_probe_gather_rows(C.c_void_p(b_ptr), n_cols, rows, fetches, i, C.c_void_p(out.data_ptr()),
+                                        C.c_void_p(stream.cuda_stream))
         b.record(stream)
         torch.cuda.synchronize()
         if rc != 0:
             return None
         if i >= 2:
             ts.append(a.elapsed_time(b))
-    return fetches * 1024.0 / (statistics.median(ts) * 1e-3) / 1e9
+    return fetches * 4.0 * n_cols / (statistics.median(ts) * 1e-3) / 1e9
 
 
 # ------------------------------------------------------------------------ CPU baseline and checker
@@ -563,16 +565,18 @@ def run_csr(args, torch, dist, R: Ranks, rank: int, world: int, local: int) -> d
     gather_gbs = gathered / (avg_step_ms * 1e-3) / 1e9
     roofline["l2_gather_gbs"] = round(gather_gbs, 1)
     # The ceiling that bounds a gather of whole B rows: a load-only probe that pulls random
-    # 1 KB rows into the SMs from an L2-resident 32 MB part of B, and the same probe over B's
-    # whole footprint (uniformly random rows, so it misses L2 more often than the kernel, whose
-    # warps walk their sorted columns together).
-    resident = gather_ceiling(torch, plan.d_B, N, min(A.cols, 32768), plan.nnz, stream)
+    # rows of B's width into the SMs from an L2-resident part of B (at most 32 MB), and the same
+    # probe over B's whole footprint (uniformly random rows, so it misses L2 more often than the
+    # kernel, whose warps walk their sorted columns together).
+    res_rows = min(A.cols, (32 << 20) // (4 * max(N, 1)))
+    resident = gather_ceiling(torch, plan.d_B, N, res_rows, plan.nnz, stream)
     same = gather_ceiling(torch, plan.d_B, N, A.cols, plan.nnz, stream)
     if resident:
         roofline["gather_ceiling"] = {
             "achieved_gbs": round(gather_gbs, 1), "ceiling_gbs": round(resident, 1),
             "frac": round(gather_gbs / resident, 4), "same_footprint_probe_gbs": round(same or 0.0, 1),
-            "probe": "load-only random 1 KB B-row fetches, L2-resident 32 MB (lib/libspmm_probe.so)"}
+            "probe": f"load-only random {4 * N}-byte B-row fetches, L2-resident {res_rows * 4 * N / 2**20:.0f} MB "
+                     "(lib/libspmm_probe.so)"}
 
     graph = graph_batch(torch, step, flops_total, S, local) if small and world == 1 else None
 

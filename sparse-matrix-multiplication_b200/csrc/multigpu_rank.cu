@@ -160,6 +160,7 @@ struct spmm_rank_plan {
     // previous run's kernels (kdone), its kernels for the previous run's copies back (end).
     cudaEvent_t kdone = nullptr;
     bool submitted = false;  // a run has been issued since the plan was made
+    bool pending = false;    // the last run was submitted and no host wait has seen it end
 
     int rows() const { return r1 - r0; }
     int nnz() const { return p1 - p0; }
@@ -299,6 +300,18 @@ int exchange_piece_issue(spmm_rank_plan* p, int j, int P, cudaStream_t s) {
         return SPMM_ERR_NCCL;
     }
     return end == ncclInProgress ? wait_comm_ready(c) : SPMM_OK;
+}
+
+// Makes `s` wait on the device for the last run's copies back when no host wait has seen them end
+// (a submitted run): kernels or copies issued on `s` next may overwrite what those copies read.
+// Inside a stream capture the wait is an external-event node of the graph.
+int order_after_last_run(spmm_rank_plan* p, cudaStream_t s) {
+    if (!p->pending) return SPMM_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    SPMM_CUDA_TRY(cudaStreamIsCapturing(s, &cs));
+    const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventWaitExternal : cudaEventWaitDefault;
+    SPMM_CUDA_TRY(cudaStreamWaitEvent(s, p->end_event(), flags));
+    return SPMM_OK;
 }
 
 int check_plan_device(const spmm_rank_plan* p) {
@@ -635,12 +648,17 @@ int spmm_rank_plan_info(const spmm_rank_plan* p, int32_t* row_begin, int32_t* ro
 int spmm_rank_run(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float* hC_rows, void* stream) {
     NvtxRange range("spmm_rank_run");
     SPMM_TRY(issue_checked(p, hA, hB, hC_rows, stream, true));
-    return wait_event(p->end_event(), p->comm, p->timeout_ms());
+    p->pending = true;
+    const int rc = wait_event(p->end_event(), p->comm, p->timeout_ms());
+    if (rc == SPMM_OK) p->pending = false;
+    return rc;
 }
 
 int spmm_rank_submit(spmm_rank_plan* p, const spmm_csr_view* hA, const float* hB, float* hC_rows, void* stream) {
     NvtxRange range("spmm_rank_submit");
-    return issue_checked(p, hA, hB, hC_rows, stream, false);
+    SPMM_TRY(issue_checked(p, hA, hB, hC_rows, stream, false));
+    p->pending = true;
+    return SPMM_OK;
 }
 
 int spmm_rank_wait(spmm_rank_plan* p, void* stream) {
@@ -648,14 +666,16 @@ int spmm_rank_wait(spmm_rank_plan* p, void* stream) {
     SPMM_TRY(check_plan_device(p));
     if (!p->submitted) return SPMM_OK;
     SPMM_CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), p->end_event(), 0));
-    return wait_event(p->end_event(), p->comm, p->timeout_ms());
+    const int rc = wait_event(p->end_event(), p->comm, p->timeout_ms());
+    if (rc == SPMM_OK) p->pending = false;
+    return rc;
 }
 
 int spmm_rank_execute(spmm_rank_plan* p, void* stream) {
     if (!p) return SPMM_ERR_INVALID_ARG;
     SPMM_TRY(check_plan_device(p));
     // On the device, after the last run's copies (it overwrites C, which they may still read).
-    if (p->submitted) SPMM_CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), p->end_event(), 0));
+    SPMM_TRY(order_after_last_run(p, as_stream(stream)));
     return spmm_csr_plan_execute(p->cplan, p->d_B, p->d_C, stream);
 }
 
@@ -663,7 +683,7 @@ int spmm_rank_gather_b(spmm_rank_plan* p, void* stream) {
     if (!p) return SPMM_ERR_INVALID_ARG;
     SPMM_TRY(check_plan_device(p));
     if (p->comm && p->comm->broken) return SPMM_ERR_NCCL;
-    if (p->submitted) SPMM_CUDA_TRY(cudaStreamWaitEvent(as_stream(stream), p->end_event(), 0));
+    SPMM_TRY(order_after_last_run(p, as_stream(stream)));
     return gather_b_issue(p, as_stream(stream));
 }
 

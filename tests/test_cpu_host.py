@@ -42,7 +42,7 @@ def test_probe_library_loads_and_exports():
 
     so = S.LIB_PATH.parent / "libspmm_probe.so"
     L = ctypes.CDLL(str(so))
-    for n in ("spmm_probe_ctas", "spmm_probe_gather"):
+    for n in ("spmm_probe_ctas", "spmm_probe_gather", "spmm_probe_gather_rows"):
         assert hasattr(L, n)
 
 

@@ -134,6 +134,38 @@ def test_execute_after_submit_waits_on_the_device(cuda):
     plan.close()
 
 
+@pytest.mark.parametrize("after", ["run", "submit"])
+def test_execute_captures_in_a_cuda_graph(cuda, after):
+    # The kernels alone captured in a CUDA graph, after a synchronous run (nothing to wait for)
+    # or after a submitted run still in flight (the wait becomes an external-event node);
+    # replayed into a NaN-filled device C they give the run's product.
+    torch = cuda
+    A, B = K.config("c2")
+    N = B.shape[1]
+    plan = S.RankPlan(None, A, N)
+    C0 = np.full((A.rows, N), np.nan, np.float32)
+    if after == "run":
+        plan.run(A, B, C0)
+    else:
+        plan.submit(A, B, C0)
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        plan.execute(side)
+    plan.wait()
+    want = expected_rows(A, B, 0, A.rows, plan.algo)
+    assert bits_equal(C0, want)
+    rt = ctypes.CDLL("libcudart.so.12")
+    assert rt.cudaMemset(ctypes.c_void_p(plan.d_C), 0xFF, ctypes.c_size_t(4 * A.rows * N)) == 0
+    graph.replay()
+    torch.cuda.synchronize()
+    assert bits_equal(device_rows(torch, plan.d_C, A.rows, N), want)
+    code, detail = S.device_error(0)
+    assert code == 0, f"device error {code} at {detail}"
+    del graph
+    plan.close()
+
+
 def test_phased_plan_runs_pipelined_and_matches(cuda):
     # B of 128 MiB (131072 x 256, about the L2) and 4.3 GB of gathers: the plan takes 3 column
     # phases for the resident launches; the pipelined end-to-end run launches its row groups
