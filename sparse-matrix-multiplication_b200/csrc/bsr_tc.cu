@@ -902,7 +902,8 @@ int spmm_bsr16_plan_create(const spmm_bsr_view* A, int32_t N, void* stream, spmm
         if (rc == SPMM_OK && p->sched) {
             const size_t ints = std::min<size_t>(p->sched_bytes / sizeof(int), (1u << 20) / sizeof(int));
             std::vector<int> host(ints);
-            if (cudaMemcpy(host.data(), p->sched, ints * sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+            if (cudaMemcpyAsync(host.data(), p->sched, ints * sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+                cudaStreamSynchronize(s) != cudaSuccess) {
                 rc = SPMM_ERR_CUDA;
             } else {
                 const int S = pick_a_stride(host, p->stride, groups, p->group);
