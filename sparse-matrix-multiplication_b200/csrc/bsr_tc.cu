@@ -211,6 +211,13 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Programmatic dependent launch: wait until the previous grid in the stream has completed and its
+// memory is visible; and let the next grid start its own setup while this one runs.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -291,6 +298,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int br0 = blockIdx.x * G;
     const int n0 = blockIdx.y * 128;
 
+    // Launched as a programmatic dependent of the previous kernel in the stream: no global memory
+    // is read or written before grid_dependency_wait(). A planned CTA's setup (barriers, TMEM)
+    // touches only shared memory and TMEM, so it overlaps the previous kernel's tail; the per-call
+    // kernel reads row pointers first, so it waits at once.
+    if constexpr (!SCHED) grid_dependency_wait();
+    if (threadIdx.x == 0) allow_dependent_launch();
+
     // Block-row extents and the group's block-column list (prefix up to kColCache); with a
     // precomputed schedule neither is needed.
     const int* my_sched = SCHED ? a.sched + static_cast<size_t>(blockIdx.x) * a.sched_stride : nullptr;
@@ -311,6 +325,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (warp == 1) tmem_alloc(sbase + L::kTmem, G * 16 <= 32 ? 32 : (G * 16 <= 64 ? 64 : 128));
     __syncthreads();
+    if constexpr (SCHED) grid_dependency_wait();
     // Monotone block-row extents.
     int lo = 0;
     if constexpr (!SCHED) {
@@ -706,9 +721,19 @@ int launch_tc_maps(const BsrArgs& a, const CUtensorMap& tb, const CUtensorMap& t
                                            L::kDynamic));
         attr_set.fetch_or(bit, std::memory_order_acq_rel);
     }
-    const dim3 grid((a.block_rows + G - 1) / G, (a.N + 127) / 128);
-    bsr_tcgen05_kernel<G, SCHED><<<grid, kTcThreads, L::kDynamic, s>>>(tb, ta, ta4, a);
-    SPMM_CUDA_TRY(cudaGetLastError());
+    // A programmatic dependent of the previous kernel in the stream (the kernel waits for it
+    // before touching global memory).
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((a.block_rows + G - 1) / G, (a.N + 127) / 128);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = L::kDynamic;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SPMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, bsr_tcgen05_kernel<G, SCHED>, tb, ta, ta4, a));
     return SPMM_OK;
 }
 
