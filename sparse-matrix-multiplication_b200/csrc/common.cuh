@@ -51,6 +51,15 @@ __device__ __forceinline__ void record_device_error(DeviceErrorRecord* rec, int 
     if (rec && atomicCAS(&rec->code, 0, code) == 0) rec->detail = detail;
 }
 
+// Programmatic dependent launch (kernels launched with programmatic stream serialisation): wait
+// until the previous grid in the stream has completed and its memory is visible -- no global
+// memory may be read or written before this -- and let the next grid launch while this one runs.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Per-device state owned by the library. Created lazily by the first call on a device;
 // that first call allocates, so it must not be made inside a stream capture.
 struct DeviceState {

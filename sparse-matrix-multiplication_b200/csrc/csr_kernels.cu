@@ -319,6 +319,10 @@ __device__ __forceinline__ void row_bounds(const CsrArgs& a, int i, int& rs, int
 
 template <int VEC, int R, int U, bool PHASED, bool HINT>
 __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_rowwarp_kernel(CsrArgs a) {
+    // A programmatic dependent of the previous kernel in the stream: its launch overlaps that
+    // kernel's tail; nothing global is touched before the wait.
+    grid_dependency_wait();
+    allow_dependent_launch();
     constexpr int W = 32 * VEC * R;
     __shared__ PairRing rings[kWarpsPerCta];
     PairRing* ring = &rings[threadIdx.x >> 5];
@@ -516,6 +520,8 @@ __device__ __forceinline__ void merge_chunk(const CsrArgs& a, PairRing* ring, in
 // runs a chunk does not change any result.
 template <int VEC, int R, int U, bool HINT, bool DYN>
 __global__ void __launch_bounds__(kThreads, SPMM_CSR_MIN_CTAS) csr_merge_kernel(CsrArgs a) {
+    grid_dependency_wait();  // a programmatic dependent launch, as csr_rowwarp_kernel
+    allow_dependent_launch();
     constexpr int W = 32 * VEC * R;
     __shared__ PairRing rings[kWarpsPerCta];
     PairRing* ring = &rings[threadIdx.x >> 5];
@@ -659,6 +665,22 @@ size_t merge_workspace_bytes(long long num_chunks, int N) {
     return counter_bytes(num_chunks, N) + static_cast<size_t>(num_chunks) * 2 * static_cast<size_t>(N) * sizeof(float);
 }
 
+// A CSR kernel launched as a programmatic dependent of the previous kernel in the stream (the
+// kernel waits for it before touching global memory). Errors surface through cudaGetLastError.
+void launch_pdl(void (*kernel)(CsrArgs), dim3 grid, cudaStream_t s, const CsrArgs& a) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    (void)cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
 template <int VEC, int R>
 void launch_vr(int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
     // Vector loads per lane in flight: U nonzeros x R strides (eight by default).
@@ -666,20 +688,20 @@ void launch_vr(int algo, const CsrArgs& a, dim3 grid, cudaStream_t s) {
     const bool hint = a.b_policy != 0;
     if (algo == SPMM_CSR_ROWWARP) {
         if (a.phases > 1) {
-            if (hint) csr_rowwarp_kernel<VEC, R, U, true, true><<<grid, kThreads, 0, s>>>(a);
-            else csr_rowwarp_kernel<VEC, R, U, true, false><<<grid, kThreads, 0, s>>>(a);
+            if (hint) launch_pdl(csr_rowwarp_kernel<VEC, R, U, true, true>, grid, s, a);
+            else launch_pdl(csr_rowwarp_kernel<VEC, R, U, true, false>, grid, s, a);
         } else {
-            if (hint) csr_rowwarp_kernel<VEC, R, U, false, true><<<grid, kThreads, 0, s>>>(a);
-            else csr_rowwarp_kernel<VEC, R, U, false, false><<<grid, kThreads, 0, s>>>(a);
+            if (hint) launch_pdl(csr_rowwarp_kernel<VEC, R, U, false, true>, grid, s, a);
+            else launch_pdl(csr_rowwarp_kernel<VEC, R, U, false, false>, grid, s, a);
         }
     } else {
         const bool dyn = a.sched_counters != nullptr;
         if (hint) {
-            if (dyn) csr_merge_kernel<VEC, R, U, true, true><<<grid, kThreads, 0, s>>>(a);
-            else csr_merge_kernel<VEC, R, U, true, false><<<grid, kThreads, 0, s>>>(a);
+            if (dyn) launch_pdl(csr_merge_kernel<VEC, R, U, true, true>, grid, s, a);
+            else launch_pdl(csr_merge_kernel<VEC, R, U, true, false>, grid, s, a);
         } else {
-            if (dyn) csr_merge_kernel<VEC, R, U, false, true><<<grid, kThreads, 0, s>>>(a);
-            else csr_merge_kernel<VEC, R, U, false, false><<<grid, kThreads, 0, s>>>(a);
+            if (dyn) launch_pdl(csr_merge_kernel<VEC, R, U, false, true>, grid, s, a);
+            else launch_pdl(csr_merge_kernel<VEC, R, U, false, false>, grid, s, a);
         }
     }
 }
